@@ -1,0 +1,79 @@
+"""Build ``libfdk.so`` (the C-ABI CUDA library) in-tree for sm_100a with nvcc.
+
+``python -m fastdecisions_b200.build`` compiles every ``csrc/*.cu`` to an object file under
+``fastdecisions_b200/_build/`` (in parallel, skipped when up to date) and links
+``fastdecisions_b200/libfdk.so``.  No GPU is needed: nvcc cross-compiles for sm_100a.
+"""
+from __future__ import annotations
+
+import concurrent.futures as cf
+import glob
+import os
+import shutil
+import subprocess
+import sys
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(PKG)
+CSRC = os.path.join(PKG, "csrc")
+BUILD = os.path.join(PKG, "_build")
+LIB = os.path.join(PKG, "libfdk.so")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found (set NVCC or put the CUDA toolkit on PATH)")
+
+
+def cutlass_include() -> str | None:
+    """CuTe/CUTLASS headers vendored by flashinfer in this image (optional, headers only)."""
+    try:
+        import flashinfer  # noqa: F401
+        d = os.path.join(os.path.dirname(flashinfer.__file__), "data", "cutlass", "include")
+        return d if os.path.isdir(d) else None
+    except Exception:
+        return None
+
+
+def _flags(extra=()):
+    f = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
+                "-I", os.path.join(ROOT, "include"), "-I", CSRC]
+    f += list(extra)
+    return f
+
+
+def _compile(src: str, obj: str, verbose_ptxas: bool) -> str:
+    deps = [src] + glob.glob(os.path.join(CSRC, "*.cuh")) + [os.path.join(ROOT, "include", "fdk.h")]
+    if os.path.exists(obj) and os.path.getmtime(obj) >= max(os.path.getmtime(d) for d in deps) and not verbose_ptxas:
+        return ""
+    cmd = [nvcc(), "-c", src, "-o", obj] + _flags(["-Xptxas", "-v"] if verbose_ptxas else [])
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nvcc failed for {os.path.basename(src)}:\n{r.stdout}\n{r.stderr}")
+    return r.stderr if verbose_ptxas else ""
+
+
+def build(verbose_ptxas: bool = False, jobs: int | None = None) -> str:
+    os.makedirs(BUILD, exist_ok=True)
+    srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+    objs = [os.path.join(BUILD, os.path.basename(s)[:-3] + ".o") for s in srcs]
+    with cf.ThreadPoolExecutor(max_workers=jobs or min(8, os.cpu_count() or 4)) as ex:
+        logs = list(ex.map(lambda so: _compile(so[0], so[1], verbose_ptxas), zip(srcs, objs)))
+    if verbose_ptxas:
+        for s, log in zip(srcs, logs):
+            print(f"== {os.path.basename(s)}\n{log}")
+    if not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
+        tmp = LIB + ".tmp"
+        cmd = [nvcc(), "-shared", "-o", tmp] + objs + ARCH + ["-Xcompiler", "-fPIC", "-lcudart"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+        os.replace(tmp, LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    print(build(verbose_ptxas="-v" in sys.argv))

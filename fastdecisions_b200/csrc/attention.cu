@@ -1,0 +1,382 @@
+// Native GQA causal attention for sm_100a: tcgen05 tensor cores, TMEM accumulators, TMA loads.
+//
+// One CTA computes a 128-query tile of TWO query heads that share one KV head (GQA pairs), so
+// every K/V tile brought into shared memory feeds two heads.  Warp roles (320 threads):
+//   warps 0-3  softmax of head A (thread = query row = TMEM lane)
+//   warps 4-7  softmax of head B
+//   warp  8    TMA producer: Q (once), K ring of 2 stages, V single stage
+//   warp  9    TMEM allocator + single-thread tcgen05.mma issuer
+// TMEM (512 columns): S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512), fp32.
+// Per KV block j the issuer runs S_A = Q_A K_j^T, S_B = Q_B K_j^T, then O_A += P_A V_j once the
+// head-A softmax has written P_A (bf16, 128B-swizzled K-major tile in shared memory), then
+// O_B += P_B V_j.  While one head's softmax runs, the tensor core works on the other head.
+// Softmax is online in fp32 in the exp2 domain with lazy rescaling of O (only when the running
+// max grows by more than 2^8).  The causal mask is applied only on the diagonal block; rows of a
+// tile past the end of its segment are computed but never stored.  Varlen: cu_seqlens gives
+// each segment's token range; nothing attends across segments.
+//
+// Every mbarrier wait is bounded (clock64 budget): on timeout the CTA raises an abort flag, all
+// roles leave their loops, in-flight MMAs and TMA loads are drained (bounded), TMEM is freed and
+// a device-side error word is set (read with fdk_poll_device_error).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <math.h>
+
+#include "common.cuh"
+#include "mma_sm80.cuh"
+#include "sm100.cuh"
+
+namespace fdk {
+namespace attn {
+using namespace sm100;
+
+constexpr int BM = 128, BN = 128, HD = 128;
+constexpr uint32_t HALF = 128 * 128;  // 128 rows x 128 B (64 bf16): one swizzle-128B box
+constexpr uint32_t TILE = 2 * HALF;   // 128 x 128 bf16
+constexpr uint32_t OFF_QA = 0, OFF_QB = TILE, OFF_K0 = 2 * TILE, OFF_K1 = 3 * TILE, OFF_V = 4 * TILE,
+                   OFF_PA = 5 * TILE, OFF_PB = 6 * TILE, OFF_BAR = 7 * TILE;
+enum { B_Q = 0, B_KF0, B_KF1, B_KE0, B_KE1, B_VF, B_VE, B_SA, B_SB, B_PA, B_PB, B_O, NBAR };
+constexpr uint32_t SMEM_BYTES = OFF_BAR + 8 * NBAR + 16 + 1024;  // + slack for 1024-B alignment
+constexpr int NUM_THREADS = 320;
+constexpr uint32_t TM_SA = 0, TM_SB = 128, TM_OA = 256, TM_OB = 384, TM_COLS = 512;
+constexpr long long DRAIN_BUDGET = 2000000000LL;
+
+__device__ int g_device_error = 0;
+
+struct Params {
+  const int32_t* cu;
+  int hq, hkv;
+  float sl2;  // softmax scale * log2(e)
+  bf16* out;
+  const bf16* gate;
+  int64_t ld_gate;
+  int gate_hstride;
+};
+
+__device__ __forceinline__ bool drain(uint32_t bar, uint32_t parity) {
+  volatile int never = 0;
+  return mbar_wait(bar, parity, &never, DRAIN_BUDGET);
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+gqa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+               const __grid_constant__ CUtensorMap tv, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t bar0 = base + OFF_BAR;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + OFF_BAR + 8 * NBAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_BAR + 8 * NBAR + 4);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int seg0 = p.cu[blockIdx.y];
+  const int L = p.cu[blockIdx.y + 1] - seg0;
+  const int mblk = (int)gridDim.x - 1 - (int)blockIdx.x;  // longest tiles first
+  const int m0 = mblk * BM;
+  if (m0 >= L) return;  // uniform early exit: this tile lies past the segment
+  const int ha = blockIdx.z * 2, hb = ha + 1;
+  const int hk = ha / (p.hq / p.hkv);
+  const int n_kv = mblk + 1;
+
+  if (tid == 0) {
+    for (int i = 0; i < NBAR; ++i) mbar_init(bar0 + 8 * i, (i == B_PA || i == B_PB) ? 128u : 1u);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(smem_u32(tmem_slot), TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&tq);
+      prefetch_tmap(&tk);
+      prefetch_tmap(&tv);
+      mbar_expect_tx(bar0 + 8 * B_Q, 2 * TILE);
+      tma_load_2d(base + OFF_QA, &tq, bar0 + 8 * B_Q, ha * HD, seg0 + m0);
+      tma_load_2d(base + OFF_QA + HALF, &tq, bar0 + 8 * B_Q, ha * HD + 64, seg0 + m0);
+      tma_load_2d(base + OFF_QB, &tq, bar0 + 8 * B_Q, hb * HD, seg0 + m0);
+      tma_load_2d(base + OFF_QB + HALF, &tq, bar0 + 8 * B_Q, hb * HD + 64, seg0 + m0);
+      int issued_k = 0, issued_v = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int ks = j & 1;
+        if (j >= 2 && !mbar_wait(bar0 + 8 * (B_KE0 + ks), ((j >> 1) - 1) & 1, abort_flag)) break;
+        const uint32_t kdst = base + (ks ? OFF_K1 : OFF_K0);
+        mbar_expect_tx(bar0 + 8 * (B_KF0 + ks), TILE);
+        tma_load_2d(kdst, &tk, bar0 + 8 * (B_KF0 + ks), hk * HD, seg0 + j * BN);
+        tma_load_2d(kdst + HALF, &tk, bar0 + 8 * (B_KF0 + ks), hk * HD + 64, seg0 + j * BN);
+        issued_k = j + 1;
+        if (j >= 1 && !mbar_wait(bar0 + 8 * B_VE, (j - 1) & 1, abort_flag)) break;
+        mbar_expect_tx(bar0 + 8 * B_VF, TILE);
+        tma_load_2d(base + OFF_V, &tv, bar0 + 8 * B_VF, hk * HD, seg0 + j * BN);
+        tma_load_2d(base + OFF_V + HALF, &tv, bar0 + 8 * B_VF, hk * HD + 64, seg0 + j * BN);
+        issued_v = j + 1;
+      }
+      // drain: every issued load must have landed before shared memory is released
+      drain(bar0 + 8 * B_Q, 0);
+      for (int j = (issued_k > 2 ? issued_k - 2 : 0); j < issued_k; ++j) drain(bar0 + 8 * (B_KF0 + (j & 1)), (j >> 1) & 1);
+      if (issued_v > 0) drain(bar0 + 8 * B_VF, (issued_v - 1) & 1);
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t ID_QK = idesc_bf16(128, 128, false, false);
+      constexpr uint32_t ID_PV = idesc_bf16(128, 128, false, true);  // V is MN-major (D contiguous)
+      bool ok = mbar_wait(bar0 + 8 * B_Q, 0, abort_flag);
+      tc_fence_after();
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int ks = j & 1;
+        if (!mbar_wait(bar0 + 8 * (B_KF0 + ks), (j >> 1) & 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t kb = base + (ks ? OFF_K1 : OFF_K0);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
+          umma_ss(tmem + TM_SA, sdesc_sw128(base + OFF_QA + off, 16, 1024), sdesc_sw128(kb + off, 16, 1024), ID_QK, kk > 0);
+        }
+        umma_commit(bar0 + 8 * B_SA);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
+          umma_ss(tmem + TM_SB, sdesc_sw128(base + OFF_QB + off, 16, 1024), sdesc_sw128(kb + off, 16, 1024), ID_QK, kk > 0);
+        }
+        umma_commit(bar0 + 8 * B_SB);
+        umma_commit(bar0 + 8 * (B_KE0 + ks));
+        if (!mbar_wait(bar0 + 8 * B_VF, j & 1, abort_flag)) break;
+        if (!mbar_wait(bar0 + 8 * B_PA, j & 1, abort_flag)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t aoff = (kk >> 2) * HALF + (kk & 3) * 32;
+          umma_ss(tmem + TM_OA, sdesc_sw128(base + OFF_PA + aoff, 16, 1024),
+                  sdesc_sw128(base + OFF_V + kk * 2048, HALF, 1024), ID_PV, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        if (!mbar_wait(bar0 + 8 * B_PB, j & 1, abort_flag)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t aoff = (kk >> 2) * HALF + (kk & 3) * 32;
+          umma_ss(tmem + TM_OB, sdesc_sw128(base + OFF_PB + aoff, 16, 1024),
+                  sdesc_sw128(base + OFF_V + kk * 2048, HALF, 1024), ID_PV, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(bar0 + 8 * B_VE);
+      }
+      umma_commit(bar0 + 8 * B_O);  // arrives when every MMA above has completed
+      drain(bar0 + 8 * B_O, 0);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax (2 warpgroups)
+    const int wg = warp >> 2;
+    const int row = (warp & 3) * 32 + lane;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_base + (wg ? TM_SB : TM_SA);
+    const uint32_t tO = tmem + lane_base + (wg ? TM_OB : TM_OA);
+    const uint32_t bS = bar0 + 8 * (wg ? B_SB : B_SA);
+    const uint32_t bP = bar0 + 8 * (wg ? B_PB : B_PA);
+    uint8_t* P = gbase + (wg ? OFF_PB : OFF_PA);
+    const float sl2 = p.sl2;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      // warp-uniform: the tcgen05.ld below is warp-collective
+      if (!__all_sync(0xffffffffu, mbar_wait(bS, j & 1, abort_flag) ? 1 : 0)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t sr[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, sr[c]);
+      tmem_ld_wait();
+      const bool diag = (j == n_kv - 1);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float v = __uint_as_float(sr[c][i]);
+          if (diag && (c * 32 + i) > row) v = -INFINITY;
+          sr[c][i] = __float_as_uint(v);
+          mx = fmaxf(mx, v);
+        }
+      const float m_new = fmaxf(m_run, mx * sl2);
+      float alpha = 1.f;
+      bool rescale = false;
+      if (j == 0) {
+        m_run = m_new;
+      } else if (m_new > m_run + 8.0f) {
+        alpha = ex2(m_run - m_new);
+        m_run = m_new;
+        rescale = true;
+      }
+      // P = exp2(S * scale * log2e - m_run) as bf16 into the swizzled K-major tile
+      float sum = 0.f;
+#pragma unroll
+      for (int c16 = 0; c16 < 16; ++c16) {
+        float e[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int col = c16 * 8 + i;
+          e[i] = ex2(fmaf(__uint_as_float(sr[col >> 5][col & 31]), sl2, -m_run));
+          sum += e[i];
+        }
+        const uint32_t off = (uint32_t)(c16 >> 3) * HALF + (uint32_t)row * 128u + ((uint32_t)((c16 & 7) ^ (row & 7)) << 4);
+        *reinterpret_cast<uint4*>(P + off) = pack8(e);
+      }
+      l_run = l_run * alpha + sum;
+      if (rescale) {  // O row *= alpha (PV of block j-1 has completed: S_j's commit covers it)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(tO + c * 32, o);
+        }
+        tmem_st_wait();
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(bP);
+    }
+    // ------------------------------------------------------------------ epilogue
+    // Warp-uniform condition: every thread of the warp saw the same waits succeed or fail.
+    if (ok && __all_sync(0xffffffffu, mbar_wait(bar0 + 8 * B_O, 0, abort_flag) ? 1 : 0)) {
+      tc_fence_after();
+      const int qpos = m0 + row;
+      const bool valid = qpos < L;
+      const int h = wg ? hb : ha;
+      const float inv_l = 1.0f / l_run;
+      const int64_t tok = (int64_t)seg0 + qpos;
+      bf16* orow = p.out + (tok * p.hq + h) * HD;
+      const bf16* grow = p.gate ? p.gate + tok * p.ld_gate + (int64_t)h * p.gate_hstride : nullptr;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tO + c * 32, o);
+        tmem_ld_wait();
+        if (valid) {
+#pragma unroll
+          for (int v8 = 0; v8 < 4; ++v8) {
+            float y[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) y[i] = __uint_as_float(o[v8 * 8 + i]) * inv_l;
+            if (grow) {
+              float gv[8];
+              unpack8(*reinterpret_cast<const uint4*>(grow + c * 32 + v8 * 8), gv);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) y[i] *= sigmoidf_(gv[i]);
+            }
+            *reinterpret_cast<uint4*>(orow + c * 32 + v8 * 8) = pack8(y);
+          }
+        }
+      }
+    }
+  }
+  // ------------------------------------------------------------------ teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TM_COLS);
+  }
+  if (tid == 0 && *abort_flag) atomicExch(&g_device_error, 1);
+}
+
+using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
+
+static EncodeFn encode_fn() {
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(ptr);
+    cudaGetLastError();
+  }
+  return fn;
+}
+
+// 2-D map over [rows, cols] bf16 (row stride ld elements), box 64 x 128, 128-byte swizzle.
+static int make_map(CUtensorMap* m, const void* ptr, int64_t cols, int64_t rows, int64_t ld) {
+  EncodeFn enc = encode_fn();
+  if (!enc) return set_error(FDK_ERR_DEVICE, "gqa_fwd: cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(FDK_ERR_INVALID_ARGUMENT, "gqa_fwd: tensor map encode failed (%d)", (int)r);
+  return FDK_OK;
+}
+
+}  // namespace attn
+}  // namespace fdk
+
+using namespace fdk;
+
+extern "C" int fdk_gqa_fwd(const void* q, int64_t ld_q, const void* k, int64_t ld_k, const void* v, int64_t ld_v,
+                           const int32_t* cu_seqlens, int64_t num_segments, int64_t max_seqlen, int64_t tokens,
+                           int64_t hq, int64_t hkv, int64_t head_dim, float scale, const void* gate, int64_t ld_gate,
+                           int gate_interleaved, void* out, void* stream) {
+  using namespace fdk::attn;
+  if (int st = check_device()) return st;
+  if (!q || !k || !v || !cu_seqlens || !out) return set_error(FDK_ERR_INVALID_ARGUMENT, "gqa_fwd: null pointer");
+  if (head_dim != HD) return set_error(FDK_ERR_UNSUPPORTED, "gqa_fwd: head_dim=%lld (128 supported)", (long long)head_dim);
+  if (hq <= 0 || hkv <= 0 || hq % hkv) return set_error(FDK_ERR_INVALID_ARGUMENT, "gqa_fwd: hq must be a multiple of hkv");
+  if ((hq / hkv) % 2) return set_error(FDK_ERR_UNSUPPORTED, "gqa_fwd: query heads per KV head must be even");
+  if (num_segments < 1 || num_segments > 65535 || tokens < 0 || max_seqlen < 0)
+    return set_error(FDK_ERR_INVALID_ARGUMENT, "gqa_fwd: bad segment count or sizes");
+  if (ld_q < hq * HD || ld_k < hkv * HD || ld_v < hkv * HD || (gate && ld_gate < hq * HD))
+    return set_error(FDK_ERR_INVALID_ARGUMENT, "gqa_fwd: row stride too small");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || ld_q % 8 || ld_k % 8 || ld_v % 8 ||
+      (gate && (!aligned16(gate) || ld_gate % 8)))
+    return set_error(FDK_ERR_ALIGNMENT, "gqa_fwd: pointers and strides must be 16-byte aligned");
+  if (tokens == 0 || max_seqlen == 0) return FDK_OK;
+  CUtensorMap mq, mk, mv;
+  if (int st = make_map(&mq, q, hq * HD, tokens, ld_q)) return st;
+  if (int st = make_map(&mk, k, hkv * HD, tokens, ld_k)) return st;
+  if (int st = make_map(&mv, v, hkv * HD, tokens, ld_v)) return st;
+  Params prm;
+  prm.cu = cu_seqlens;
+  prm.hq = (int)hq;
+  prm.hkv = (int)hkv;
+  prm.sl2 = scale * 1.4426950408889634f;
+  prm.out = static_cast<bf16*>(out);
+  prm.gate = static_cast<const bf16*>(gate);
+  prm.ld_gate = ld_gate;
+  prm.gate_hstride = gate_interleaved ? 2 * HD : HD;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaFuncSetAttribute(gqa_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  const int64_t mtiles = (max_seqlen + BM - 1) / BM;
+  dim3 grid((unsigned)mtiles, (unsigned)num_segments, (unsigned)(hq / 2));
+  gqa_fwd_kernel<<<grid, NUM_THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(mq, mk, mv, prm);
+  return check_launch("gqa_fwd");
+}
+
+extern "C" int fdk_poll_device_error(int* code) {
+  int h = 0;
+  if (cudaMemcpyFromSymbol(&h, fdk::attn::g_device_error, sizeof(int)) != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(FDK_ERR_DEVICE, "poll_device_error: cannot read the device error word");
+  }
+  if (h) {
+    int zero = 0;
+    cudaMemcpyToSymbol(fdk::attn::g_device_error, &zero, sizeof(int));
+  }
+  if (code) *code = h;
+  return FDK_OK;
+}

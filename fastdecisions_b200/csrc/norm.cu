@@ -1,0 +1,281 @@
+// Normalisation kernels of the decoder: fused residual add + RMSNorm (1 + w), the GDN gated
+// RMSNorm and the attention q/k RMSNorm + partial RoPE prologue.  All HBM-bound: every input
+// byte is read once with 16-byte vector loads and every output byte written once.
+#include "common.cuh"
+
+namespace fdk {
+
+// ---------------------------------------------------------------------------------------------
+// Residual add + RMSNorm: one row per 128-thread warp group; each thread keeps its NC 8-wide
+// chunks of the row in registers between the sum-of-squares pass and the scaling pass.
+// ---------------------------------------------------------------------------------------------
+template <int NC, bool HAS_RES, bool W_FP32>
+__global__ void __launch_bounds__(128) residual_rmsnorm_kernel(
+    const bf16* __restrict__ x, int64_t ldx, const bf16* __restrict__ res, int64_t ldr,
+    const void* __restrict__ w, bf16* __restrict__ out, int64_t ldo, bf16* __restrict__ res_out,
+    int64_t ldro, int hidden, float eps, float woff) {
+  const int64_t row = blockIdx.x;
+  const int nvec = hidden >> 3;
+  const bf16* xr = x + row * ldx;
+  const bf16* rr = HAS_RES ? res + row * ldr : nullptr;
+  float v[NC][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int i = threadIdx.x + c * 128;
+    if (i < nvec) {
+      uint4 ux = ldg_stream(xr + i * 8);
+      unpack8(ux, v[c]);
+      if (HAS_RES) {
+        float r8[8];
+        uint4 ur = ldg_stream(rr + i * 8);
+        unpack8(ur, r8);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[c][j] = round_bf16(v[c][j] + r8[j]);  // s is stored in bf16
+        if (res_out != nullptr) *reinterpret_cast<uint4*>(res_out + row * ldro + i * 8) = pack8(v[c]);
+      } else if (res_out != nullptr) {
+        *reinterpret_cast<uint4*>(res_out + row * ldro + i * 8) = ux;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(v[c][j], v[c][j], ss);
+    }
+  }
+  __shared__ float red[4];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  ss = (red[0] + red[1]) + (red[2] + red[3]);
+  const float inv = rsqrtf(ss / (float)hidden + eps);
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int i = threadIdx.x + c * 128;
+    if (i < nvec) {
+      float wv[8];
+      if (W_FP32) {
+        const float4* wp = reinterpret_cast<const float4*>(static_cast<const float*>(w) + i * 8);
+        float4 a = __ldg(wp), b = __ldg(wp + 1);
+        wv[0] = a.x; wv[1] = a.y; wv[2] = a.z; wv[3] = a.w;
+        wv[4] = b.x; wv[5] = b.y; wv[6] = b.z; wv[7] = b.w;
+      } else {
+        uint4 uw = __ldg(reinterpret_cast<const uint4*>(static_cast<const bf16*>(w) + i * 8));
+        unpack8(uw, wv);
+      }
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = v[c][j] * inv * (woff + wv[j]);
+      *reinterpret_cast<uint4*>(out + row * ldo + i * 8) = pack8(o);
+    }
+  }
+}
+
+template <int NC>
+static void launch_rms(bool has_res, bool w32, dim3 grid, cudaStream_t s, const bf16* x, int64_t ldx,
+                       const bf16* r, int64_t ldr, const void* w, bf16* o, int64_t ldo, bf16* ro,
+                       int64_t ldro, int hidden, float eps, float woff) {
+  if (has_res) {
+    if (w32) residual_rmsnorm_kernel<NC, true, true><<<grid, 128, 0, s>>>(x, ldx, r, ldr, w, o, ldo, ro, ldro, hidden, eps, woff);
+    else     residual_rmsnorm_kernel<NC, true, false><<<grid, 128, 0, s>>>(x, ldx, r, ldr, w, o, ldo, ro, ldro, hidden, eps, woff);
+  } else {
+    if (w32) residual_rmsnorm_kernel<NC, false, true><<<grid, 128, 0, s>>>(x, ldx, r, ldr, w, o, ldo, ro, ldro, hidden, eps, woff);
+    else     residual_rmsnorm_kernel<NC, false, false><<<grid, 128, 0, s>>>(x, ldx, r, ldr, w, o, ldo, ro, ldro, hidden, eps, woff);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Gated RMSNorm per head row (dv = 128): 16 lanes per row, one 16-byte chunk of o and z each.
+// ---------------------------------------------------------------------------------------------
+template <bool W_FP32>
+__global__ void __launch_bounds__(256) gated_rmsnorm_kernel(
+    const bf16* __restrict__ o, const bf16* __restrict__ z, int64_t ldz, const void* __restrict__ w,
+    bf16* __restrict__ out, int64_t rows, int heads, float eps) {
+  const int64_t row = (int64_t)blockIdx.x * 16 + (threadIdx.x >> 4);  // row = token * heads + head
+  const int lane = threadIdx.x & 15;
+  if (row >= rows) return;
+  const int64_t t = row / heads;
+  const int h = (int)(row - t * heads);
+  float ov[8], zv[8], wv[8];
+  unpack8(ldg_stream(o + row * 128 + lane * 8), ov);
+  unpack8(ldg_stream(z + t * ldz + (int64_t)h * 128 + lane * 8), zv);
+  if (W_FP32) {
+    const float* wp = static_cast<const float*>(w) + lane * 8;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) wv[j] = __ldg(wp + j);
+  } else {
+    unpack8(__ldg(reinterpret_cast<const uint4*>(static_cast<const bf16*>(w) + lane * 8)), wv);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) ss = fmaf(ov[j], ov[j], ss);
+#pragma unroll
+  for (int m = 8; m > 0; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+  const float inv = rsqrtf(ss * (1.0f / 128.0f) + eps);
+  float r[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) r[j] = wv[j] * (ov[j] * inv) * silu(zv[j]);
+  *reinterpret_cast<uint4*>(out + row * 128 + lane * 8) = pack8(r);
+}
+
+// ---------------------------------------------------------------------------------------------
+// q/k RMSNorm (1 + w) over head_dim + partial rotary embedding.  One warp per (token, head) row;
+// lane l holds features [l*E, l*E + E) with E = head_dim / 32 (4 for 128, 8 for 256).
+// rotate_half pairs feature i with i + rot/2 inside the first rot features.
+// ---------------------------------------------------------------------------------------------
+template <int E, bool W_FP32>
+__global__ void __launch_bounds__(256) qk_norm_rope_kernel(
+    const bf16* __restrict__ qkv, int64_t ldq, const void* __restrict__ qw, const void* __restrict__ kw,
+    const int32_t* __restrict__ pos, const float* __restrict__ inv_freq, int rot, bf16* __restrict__ qo,
+    bf16* __restrict__ ko, int64_t tokens, int hq, int hkv, float eps) {
+  constexpr int D = E * 32;
+  const int64_t gw = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int64_t rows_per_tok = hq + hkv;
+  if (gw >= tokens * rows_per_tok) return;
+  const int64_t t = gw / rows_per_tok;
+  const int r = (int)(gw - t * rows_per_tok);
+  const bool is_q = r < hq;
+  const bf16* src = is_q ? qkv + t * ldq + (int64_t)r * 2 * D : qkv + t * ldq + (int64_t)hq * 2 * D + (int64_t)(r - hq) * D;
+  bf16* dst = is_q ? qo + (t * hq + r) * D : ko + (t * hkv + (r - hq)) * D;
+  const void* w = is_q ? qw : kw;
+  float x[E];
+  if (E == 4) {
+    uint2 u = *reinterpret_cast<const uint2*>(src + lane * 4);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+    float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+    x[0] = a.x; x[1] = a.y; x[2] = b.x; x[3] = b.y;
+  } else {
+    float tmp[8];
+    unpack8(*reinterpret_cast<const uint4*>(src + lane * 8), tmp);
+#pragma unroll
+    for (int j = 0; j < E; ++j) x[j] = tmp[j];
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < E; ++j) ss = fmaf(x[j], x[j], ss);
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / (float)D + eps);
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    const int f = lane * E + j;
+    float wf = W_FP32 ? __ldg(static_cast<const float*>(w) + f) : __bfloat162float(static_cast<const bf16*>(w)[f]);
+    x[j] = x[j] * inv * (1.0f + wf);
+  }
+  // partner lane holding feature f +/- rot/2 (rot/2 is a multiple of E since rot % 8 == 0 and E <= 8)
+  const int half = rot >> 1;
+  const int lane_off = half / E;
+  const float p = (float)pos[t];
+  float y[E];
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    const int f = lane * E + j;
+    const int src_lane = (f < half) ? lane + lane_off : lane - lane_off;
+    float partner = __shfl_sync(0xffffffffu, x[j], src_lane < 0 ? 0 : (src_lane > 31 ? 31 : src_lane));
+    if (f < rot) {
+      float sn, cs;
+      sincosf(p * inv_freq[f % half], &sn, &cs);
+      const float rotv = (f < half) ? -partner : partner;
+      y[j] = x[j] * cs + rotv * sn;
+    } else {
+      y[j] = x[j];
+    }
+  }
+  if (E == 4) {
+    uint2 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+    h[0] = __floats2bfloat162_rn(y[0], y[1]);
+    h[1] = __floats2bfloat162_rn(y[2], y[3]);
+    *reinterpret_cast<uint2*>(dst + lane * 4) = u;
+  } else {
+    float tmp[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) tmp[j] = y[j % E];
+    *reinterpret_cast<uint4*>(dst + lane * 8) = pack8(tmp);
+  }
+}
+
+}  // namespace fdk
+
+using namespace fdk;
+
+extern "C" int fdk_residual_rmsnorm(const void* x, int64_t ld_x, const void* residual, int64_t ld_residual,
+                                    const void* weight, int weight_is_fp32, void* out, int64_t ld_out,
+                                    void* residual_out, int64_t ld_residual_out, int64_t rows, int64_t hidden,
+                                    float eps, float weight_offset, void* stream) {
+  if (int st = check_device()) return st;
+  if (!x || !weight || !out) return set_error(FDK_ERR_INVALID_ARGUMENT, "residual_rmsnorm: null pointer");
+  if (rows < 0 || hidden <= 0 || hidden % 8 != 0 || hidden > 8192)
+    return set_error(FDK_ERR_UNSUPPORTED, "residual_rmsnorm: hidden=%lld must be a positive multiple of 8 <= 8192", (long long)hidden);
+  if (ld_x < hidden || ld_out < hidden || (residual && ld_residual < hidden) || (residual_out && ld_residual_out < hidden))
+    return set_error(FDK_ERR_INVALID_ARGUMENT, "residual_rmsnorm: row stride smaller than hidden");
+  if (!aligned16(x) || !aligned16(out) || (residual && !aligned16(residual)) || (residual_out && !aligned16(residual_out)) ||
+      !aligned16(weight) || ld_x % 8 || ld_out % 8 || (residual && ld_residual % 8) || (residual_out && ld_residual_out % 8))
+    return set_error(FDK_ERR_ALIGNMENT, "residual_rmsnorm: pointers and row strides must be 16-byte aligned");
+  if (rows == 0) return FDK_OK;
+  if (rows > 0x7fffffff) return set_error(FDK_ERR_UNSUPPORTED, "residual_rmsnorm: too many rows");
+  dim3 grid((unsigned)rows);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int nc = (int)((hidden / 8 + 127) / 128);
+  auto xb = static_cast<const bf16*>(x);
+  auto rb = static_cast<const bf16*>(residual);
+  auto ob = static_cast<bf16*>(out);
+  auto rob = static_cast<bf16*>(residual_out);
+  bool hr = residual != nullptr, w32 = weight_is_fp32 != 0;
+  switch (nc) {
+    case 1: launch_rms<1>(hr, w32, grid, s, xb, ld_x, rb, ld_residual, weight, ob, ld_out, rob, ld_residual_out, (int)hidden, eps, weight_offset); break;
+    case 2: launch_rms<2>(hr, w32, grid, s, xb, ld_x, rb, ld_residual, weight, ob, ld_out, rob, ld_residual_out, (int)hidden, eps, weight_offset); break;
+    case 3:
+    case 4: launch_rms<4>(hr, w32, grid, s, xb, ld_x, rb, ld_residual, weight, ob, ld_out, rob, ld_residual_out, (int)hidden, eps, weight_offset); break;
+    default: launch_rms<8>(hr, w32, grid, s, xb, ld_x, rb, ld_residual, weight, ob, ld_out, rob, ld_residual_out, (int)hidden, eps, weight_offset); break;
+  }
+  return check_launch("residual_rmsnorm");
+}
+
+extern "C" int fdk_gated_rmsnorm(const void* o, const void* z, int64_t ld_z, const void* weight, int weight_is_fp32,
+                                 void* out, int64_t tokens, int64_t heads, int64_t dv, float eps, void* stream) {
+  if (int st = check_device()) return st;
+  if (!o || !z || !weight || !out) return set_error(FDK_ERR_INVALID_ARGUMENT, "gated_rmsnorm: null pointer");
+  if (dv != 128) return set_error(FDK_ERR_UNSUPPORTED, "gated_rmsnorm: dv=%lld (only 128 supported)", (long long)dv);
+  if (tokens < 0 || heads <= 0 || ld_z < heads * dv) return set_error(FDK_ERR_INVALID_ARGUMENT, "gated_rmsnorm: bad sizes");
+  if (!aligned16(o) || !aligned16(z) || !aligned16(out) || ld_z % 8 || !aligned16(weight))
+    return set_error(FDK_ERR_ALIGNMENT, "gated_rmsnorm: pointers and strides must be 16-byte aligned");
+  const int64_t rows = tokens * heads;
+  if (rows == 0) return FDK_OK;
+  dim3 grid((unsigned)((rows + 15) / 16));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (weight_is_fp32)
+    gated_rmsnorm_kernel<true><<<grid, 256, 0, s>>>(static_cast<const bf16*>(o), static_cast<const bf16*>(z), ld_z, weight, static_cast<bf16*>(out), rows, (int)heads, eps);
+  else
+    gated_rmsnorm_kernel<false><<<grid, 256, 0, s>>>(static_cast<const bf16*>(o), static_cast<const bf16*>(z), ld_z, weight, static_cast<bf16*>(out), rows, (int)heads, eps);
+  return check_launch("gated_rmsnorm");
+}
+
+extern "C" int fdk_attn_qk_norm_rope(const void* qkv, int64_t ld_qkv, const void* q_norm_w, const void* k_norm_w,
+                                     int weight_is_fp32, const int32_t* positions, const float* inv_freq, int rot_dim,
+                                     void* q_out, void* k_out, int64_t tokens, int64_t hq, int64_t hkv, int64_t head_dim,
+                                     float eps, void* stream) {
+  if (int st = check_device()) return st;
+  if (!qkv || !q_norm_w || !k_norm_w || !positions || !inv_freq || !q_out || !k_out)
+    return set_error(FDK_ERR_INVALID_ARGUMENT, "attn_qk_norm_rope: null pointer");
+  if (head_dim != 128 && head_dim != 256)
+    return set_error(FDK_ERR_UNSUPPORTED, "attn_qk_norm_rope: head_dim=%lld (128 or 256)", (long long)head_dim);
+  if (rot_dim <= 0 || rot_dim > head_dim || rot_dim % 8 != 0 || (rot_dim / 2) % (head_dim / 32) != 0)
+    return set_error(FDK_ERR_UNSUPPORTED, "attn_qk_norm_rope: rot_dim=%d unsupported", rot_dim);
+  if (tokens < 0 || hq <= 0 || hkv <= 0 || ld_qkv < (2 * hq + hkv) * head_dim)
+    return set_error(FDK_ERR_INVALID_ARGUMENT, "attn_qk_norm_rope: bad sizes");
+  if (!aligned16(qkv) || ld_qkv % 8 || !aligned16(q_out) || !aligned16(k_out))
+    return set_error(FDK_ERR_ALIGNMENT, "attn_qk_norm_rope: pointers and strides must be 16-byte aligned");
+  const int64_t rows = tokens * (hq + hkv);
+  if (rows == 0) return FDK_OK;
+  dim3 grid((unsigned)((rows + 7) / 8));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto in = static_cast<const bf16*>(qkv);
+  auto qo = static_cast<bf16*>(q_out);
+  auto ko = static_cast<bf16*>(k_out);
+  if (head_dim == 128) {
+    if (weight_is_fp32) qk_norm_rope_kernel<4, true><<<grid, 256, 0, s>>>(in, ld_qkv, q_norm_w, k_norm_w, positions, inv_freq, rot_dim, qo, ko, tokens, (int)hq, (int)hkv, eps);
+    else qk_norm_rope_kernel<4, false><<<grid, 256, 0, s>>>(in, ld_qkv, q_norm_w, k_norm_w, positions, inv_freq, rot_dim, qo, ko, tokens, (int)hq, (int)hkv, eps);
+  } else {
+    if (weight_is_fp32) qk_norm_rope_kernel<8, true><<<grid, 256, 0, s>>>(in, ld_qkv, q_norm_w, k_norm_w, positions, inv_freq, rot_dim, qo, ko, tokens, (int)hq, (int)hkv, eps);
+    else qk_norm_rope_kernel<8, false><<<grid, 256, 0, s>>>(in, ld_qkv, q_norm_w, k_norm_w, positions, inv_freq, rot_dim, qo, ko, tokens, (int)hq, (int)hkv, eps);
+  }
+  return check_launch("attn_qk_norm_rope");
+}

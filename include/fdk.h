@@ -1,0 +1,202 @@
+/*
+ * fastdecisions-b200 C ABI: the drop-in boundary for the forward hot path of the FastDecisions
+ * one-pass decision model (a Qwen3.5-style hybrid decoder: Gated-DeltaNet linear-attention layers
+ * and gated GQA attention layers), built for NVIDIA B200 (sm_100a).
+ *
+ * Conventions (all entry points):
+ *   - Plain device pointers, element counts and strides (in elements), no framework types.
+ *   - Tensors are bf16 (__nv_bfloat16 bit patterns) unless a parameter says float32/int32.
+ *   - `stream` is a cudaStream_t (may be NULL for the legacy default stream).  Every entry point
+ *     only enqueues work: no allocation, no host synchronisation, a fixed launch configuration for
+ *     a given shape, so calls can be captured into CUDA graphs.
+ *   - Return value: FDK_OK (0) or one of the FDK_ERR_* codes below; fdk_get_last_error_string()
+ *     then describes the failure (thread-local).  The library never aborts the process.
+ *   - The library never allocates device memory.  Scratch space, where an op needs it, is passed
+ *     in by the caller (see fdk_chunk_gated_delta_rule_workspace_size).
+ *
+ * Reference interfaces each entry point replaces are cited as file:line of the FastDecisions
+ * repository (src/decider/...) or of transformers 5.5.0 models/qwen3_5/modeling_qwen3_5.py
+ * (written [tf]:line), which holds the model arithmetic the reference calls.
+ */
+#ifndef FASTDECISIONS_B200_FDK_H_
+#define FASTDECISIONS_B200_FDK_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FDK_OK 0
+#define FDK_ERR_INVALID_ARGUMENT 1 /* bad shape, size, null pointer or stride                  */
+#define FDK_ERR_ALIGNMENT 2        /* a pointer or stride breaks the 16-byte alignment rule       */
+#define FDK_ERR_UNSUPPORTED 3      /* valid request outside what the kernels implement           */
+#define FDK_ERR_LAUNCH 4           /* the CUDA launch itself failed                               */
+#define FDK_ERR_DEVICE 5           /* no CUDA device, or the device is not sm_100               */
+
+/* Library version string, e.g. "fastdecisions-b200 0.1.0 sm_100a". */
+const char* fdk_version(void);
+
+/* Message for the last non-zero status returned on this host thread. */
+const char* fdk_get_last_error_string(void);
+
+/*
+ * Fused residual add + Qwen3.5 RMSNorm (one row per 128-thread warp group).
+ * Replaces `fastdecisions::residual_rms(a, b, weight)` (src/decider/persistent_residual_rms.py:7-14,
+ * launcher persistent_residual_rms_kernel.py:75-104) with the eager semantics of
+ * [tf]:711-728 + [tf]:775-779:
+ *     s   = bf16(x + residual)                 (s = x when residual == NULL)
+ *     out = bf16(s * rsqrt(mean(s^2) + eps) * (weight_offset + w))
+ * and also writes s to residual_out when it is non-NULL (the reference kernel omits eps and
+ * never writes s).  weight is bf16, or float32 when weight_is_fp32 != 0.  Row strides ld_* are
+ * in elements and must keep every row 16-byte aligned; hidden % 8 == 0, hidden <= 8192.
+ */
+int fdk_residual_rmsnorm(const void* x, int64_t ld_x, const void* residual, int64_t ld_residual,
+                         const void* weight, int weight_is_fp32, void* out, int64_t ld_out,
+                         void* residual_out, int64_t ld_residual_out, int64_t rows, int64_t hidden,
+                         float eps, float weight_offset, void* stream);
+
+/*
+ * Packed depthwise causal conv1d (width kernel_width <= 4, zero left padding) + SiLU that writes
+ * q, k, v directly in the [B, T, H, D] layout the delta rule reads.
+ * Replaces `fastdecisions::packed_conv(x, weight)` (src/decider/packed_conv.py:12-21, launcher
+ * packed_conv_kernel.py:194-232 `prep_qkv`), generalised from T=2048/C=6144 to any T and
+ * C = 2*key_dim + value_dim, plus packed varlen input:
+ *     x: [batch, seqlen, C] with row stride ld_x; weight: [C, kernel_width] bf16 contiguous
+ *     cu_seqlens: NULL (dense batch) or int32 [num_segments + 1] device array over the flattened
+ *                 tokens (batch must be 1); each segment starts with a zero history.
+ *     q, k: [batch*seqlen, key_dim], v: [batch*seqlen, value_dim], contiguous.
+ */
+int fdk_packed_conv_silu(const void* x, int64_t ld_x, const void* weight, int64_t batch,
+                         int64_t seqlen, int64_t channels, int kernel_width,
+                         const int32_t* cu_seqlens, int64_t num_segments, int64_t key_dim,
+                         int64_t value_dim, void* q, void* k, void* v, void* stream);
+
+/*
+ * Gated-DeltaNet gate transform:  g = -exp(A_log) * softplus(a + dt_bias)  (float32 out),
+ * beta = sigmoid(b) (bf16 out).  Replaces `fastdecisions::unpack_gate` (src/decider/
+ * combined_gates.py:6-16, kernel unpack_gate_transform_kernel.py:52-89) and [tf]:491-493.
+ * a, b: [tokens, heads] with row strides ld_a, ld_b (elements); A_log, dt_bias: float32 [heads].
+ * g: float32 [tokens, heads]; beta: bf16 [tokens, heads], contiguous.
+ */
+int fdk_gdn_gates(const void* a, int64_t ld_a, const void* b, int64_t ld_b, const float* A_log,
+                  const float* dt_bias, float* g, void* beta, int64_t tokens, int64_t heads,
+                  void* stream);
+
+/*
+ * Scratch bytes fdk_chunk_gated_delta_rule_fwd needs for `tokens` packed tokens split into
+ * `num_segments` sequences with `heads` heads of key dim dk and value dim dv.
+ */
+size_t fdk_chunk_gated_delta_rule_workspace_size(int64_t tokens, int64_t num_segments,
+                                                 int64_t heads, int64_t dk, int64_t dv);
+
+/*
+ * Chunked gated delta rule (chunk 64), the linear-attention core of the GDN layer.
+ * Replaces transformers' `torch_chunk_gated_delta_rule` / fla `chunk_gated_delta_rule`
+ * ([tf]:234-311, called at [tf]:499-508 and src/decider/packed_conv.py:55-59) with
+ * use_qk_l2norm_in_kernel=True semantics:
+ *     q, k: [tokens, heads, dk] bf16 (row stride ld_qk elements per token);
+ *     v: [tokens, heads, dv] bf16 (row stride ld_v);
+ *     g: float32 [tokens, heads] (per-token log decay), beta: bf16 [tokens, heads];
+ *     cu_seqlens: int32 [num_segments + 1] device array (tokens = cu_seqlens[num_segments]);
+ *     initial_state: NULL or float32 [num_segments, heads, dk, dv];
+ *     out: [tokens, heads, dv] bf16 contiguous; final_state: NULL or float32
+ *          [num_segments, heads, dk, dv];
+ *     workspace: caller-owned device scratch of at least
+ *                fdk_chunk_gated_delta_rule_workspace_size(...) bytes, 256-byte aligned.
+ * Supports dk == dv == 128.  Internally fp32 for the l2 norms, the decay cumsum, the
+ * unit-lower-triangular solve and the recurrent state; bf16 tensor-core products with fp32
+ * accumulation for the chunk matmuls.
+ */
+int fdk_chunk_gated_delta_rule_fwd(const void* q, const void* k, int64_t ld_qk, const void* v,
+                                   int64_t ld_v, const float* g, const void* beta,
+                                   const int32_t* cu_seqlens, int64_t num_segments,
+                                   int64_t tokens, int64_t heads, int64_t dk, int64_t dv,
+                                   float scale, const float* initial_state, void* out,
+                                   float* final_state, void* workspace, size_t workspace_bytes,
+                                   void* stream);
+
+/*
+ * Gated RMSNorm of the GDN output, per head row of width dv:
+ *     out = bf16(w * (o * rsqrt(mean(o^2) + eps)) * silu(z))
+ * Replaces Qwen3_5RMSNormGated / fla FusedRMSNormGated ([tf]:175-190, call site [tf]:526-529).
+ * o: [tokens, heads, dv] contiguous; z: [tokens, heads*dv] with row stride ld_z;
+ * weight: [dv] bf16 (weight_is_fp32 = 0) or float32; out: [tokens, heads*dv] contiguous.
+ */
+int fdk_gated_rmsnorm(const void* o, const void* z, int64_t ld_z, const void* weight,
+                      int weight_is_fp32, void* out, int64_t tokens, int64_t heads, int64_t dv,
+                      float eps, void* stream);
+
+/*
+ * Attention-layer prologue: q_norm / k_norm (Qwen3.5 RMSNorm with 1+w over head_dim) and partial
+ * rotary embedding of the first rot_dim features ([tf]:657-668; patched form
+ * experiments/native_gqa/bench_native_gqa_model.py:43-53).
+ *     qkv: [tokens, ld_qkv] projection output laid out as q_proj ([hq, 2, head_dim]: query then
+ *          output gate per head) followed by k_proj [hkv, head_dim] (v_proj after it is untouched)
+ *     positions: int32 [tokens] (position within the request); inv_freq: float32 [rot_dim/2]
+ *     q_out: [tokens, hq, head_dim], k_out: [tokens, hkv, head_dim] contiguous.
+ * Supports head_dim == 128 or 256 and rot_dim <= head_dim, rot_dim % 8 == 0.
+ */
+int fdk_attn_qk_norm_rope(const void* qkv, int64_t ld_qkv, const void* q_norm_w,
+                          const void* k_norm_w, int weight_is_fp32, const int32_t* positions,
+                          const float* inv_freq, int rot_dim, void* q_out, void* k_out,
+                          int64_t tokens, int64_t hq, int64_t hkv, int64_t head_dim, float eps,
+                          void* stream);
+
+/*
+ * Native GQA causal attention, tcgen05 tensor cores with TMEM accumulators fed by TMA.
+ * Replaces `native_gqa_attention(q, k, v)` (src/decider/native_gqa_kernel.py:116-173) and the
+ * SDPA path with repeat_kv ([tf]:582-617): query head h reads KV head h / (hq / hkv) directly.
+ *     q: [tokens, hq, head_dim] (token stride ld_q elements, head stride head_dim);
+ *     k, v: [tokens, hkv, head_dim] (token strides ld_k, ld_v);
+ *     cu_seqlens: int32 [num_segments + 1] device array (packed varlen; causal inside each
+ *                 segment, no attention across segments); max_seqlen bounds the longest segment;
+ *     gate: NULL, or [tokens, hq*head_dim] with row stride ld_gate (and head stride 2*head_dim
+ *           when gate_interleaved != 0): out = attn * sigmoid(gate) ([tf]:687-689) fused;
+ *     out: [tokens, hq, head_dim] contiguous bf16.
+ * Softmax statistics are float32 (online, exp2 domain); P is rounded to bf16 before P.V.
+ * Supports head_dim == 128; all strides must be multiples of 8 elements (16-byte TMA rule).
+ */
+int fdk_gqa_fwd(const void* q, int64_t ld_q, const void* k, int64_t ld_k, const void* v,
+                int64_t ld_v, const int32_t* cu_seqlens, int64_t num_segments,
+                int64_t max_seqlen, int64_t tokens, int64_t hq, int64_t hkv, int64_t head_dim,
+                float scale, const void* gate, int64_t ld_gate, int gate_interleaved, void* out,
+                void* stream);
+
+/*
+ * Reads and clears the device-side error word of the current device.  Kernels that wait on
+ * mbarriers (fdk_gqa_fwd) bound every wait; a wait that runs out sets this word to non-zero,
+ * frees its resources and returns without finishing its tile.  Synchronises with the device.
+ * No reference counterpart (the reference's Triton kernels have no device waits).
+ */
+int fdk_poll_device_error(int* code);
+
+/* Token embedding gather: out[t, :] = table[ids[t], :] ([tf]:1243).  ids int32. */
+int fdk_embed(const int32_t* ids, const void* table, int64_t vocab, int64_t hidden, void* out,
+              int64_t tokens, void* stream);
+
+/* SwiGLU: out[t, i] = bf16(silu(gu[t, i]) * gu[t, inter + i]) ([tf]:706-708); gu row stride
+ * ld_gu (elements), out [tokens, inter] contiguous. */
+int fdk_swiglu(const void* gu, int64_t ld_gu, void* out, int64_t tokens, int64_t inter,
+               void* stream);
+
+/*
+ * Slot readout: final RMSNorm (1+w) of the slot rows, restricted logits over `num_letters`
+ * candidate rows and a masked, temperature-scaled softmax.  Replaces the slot gather,
+ * F.linear(h, W_letters) and read_slots/scaled_softmax of src/decider/model.py:18-27 and
+ * src/decider/engine.py:48-56 (temperature.py:136-144).
+ *     hidden: [tokens, hidden_size] (residual stream after the last layer);
+ *     slots, nopts: int32 [num_slots]; letters: [num_letters, hidden_size] bf16;
+ *     probs, logits: float32 [num_slots, num_letters] (options >= nopts get p = 0, logit -inf).
+ */
+int fdk_slot_readout(const void* hidden, int64_t hidden_size, const int32_t* slots,
+                     const int32_t* nopts, int64_t num_slots, const void* final_norm_w,
+                     int weight_is_fp32, const void* letters, int64_t num_letters, float eps,
+                     float temperature, float* probs, float* logits, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FASTDECISIONS_B200_FDK_H_ */

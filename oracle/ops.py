@@ -178,11 +178,12 @@ def chunk_gated_delta_rule(query, key, value, g, beta, chunk_size: int = 64, ini
     for b in range(B):
         segs = _segments(T, cu_seqlens) if cu_seqlens is not None else [(0, T)]
         for si, (s0, s1) in enumerate(segs):
-            if s1 <= s0:
-                continue
             st = None
             if initial_state is not None:
                 st = _f(initial_state[si if cu_seqlens is not None else b])
+            if s1 <= s0:  # an empty request keeps its initial (or zero) state
+                states.append(st if st is not None else torch.zeros(H, k.shape[-1], v.shape[-1]))
+                continue
             o, S = _chunk_delta_one(q[b, s0:s1].transpose(0, 1), k[b, s0:s1].transpose(0, 1),
                                     v[b, s0:s1].transpose(0, 1), gg[b, s0:s1].transpose(0, 1),
                                     bb[b, s0:s1].transpose(0, 1), chunk_size, st)
