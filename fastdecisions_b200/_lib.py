@@ -26,7 +26,7 @@ vp, i64, i32, f32, sz = C.c_void_p, C.c_int64, C.c_int, C.c_float, C.c_size_t
 SIGNATURES = {
     "fdk_version": (C.c_char_p, []),
     "fdk_get_last_error_string": (C.c_char_p, []),
-    "fdk_residual_rmsnorm": (i32, [vp, i64, vp, i64, vp, i32, vp, i64, vp, i64, i64, i64, f32, f32, vp]),
+    "fdk_residual_rmsnorm": (i32, [vp, i64, vp, i64, i32, vp, i32, vp, i64, vp, i64, i64, i64, f32, f32, vp]),
     "fdk_packed_conv_silu": (i32, [vp, i64, vp, i64, i64, i64, i32, vp, i64, i64, i64, vp, vp, vp, vp]),
     "fdk_gdn_gates": (i32, [vp, i64, vp, i64, vp, vp, vp, vp, i64, i64, vp]),
     "fdk_chunk_gated_delta_rule_workspace_size": (sz, [i64, i64, i64, i64, i64]),
@@ -38,7 +38,7 @@ SIGNATURES = {
     "fdk_poll_device_error": (i32, [C.POINTER(C.c_int)]),
     "fdk_embed": (i32, [vp, vp, i64, i64, vp, i64, vp]),
     "fdk_swiglu": (i32, [vp, i64, vp, i64, i64, vp]),
-    "fdk_slot_readout": (i32, [vp, i64, vp, vp, i64, vp, i32, vp, i64, f32, f32, vp, vp, vp]),
+    "fdk_slot_readout": (i32, [vp, i32, vp, i64, vp, vp, i64, vp, i32, vp, i64, f32, f32, vp, vp, vp]),
 }
 
 _lib = None

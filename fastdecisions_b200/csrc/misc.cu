@@ -46,18 +46,26 @@ __global__ void swiglu_kernel(const bf16* __restrict__ gu, int64_t ldgu, bf16* _
 
 // One 256-thread block per slot: RMSNorm (1 + w) of the slot row, K <= 16 restricted logits,
 // masked softmax(logits / temperature).
-template <bool W_FP32>
+constexpr int READOUT_MAX_H = 8192;
+
+template <bool W_FP32, bool HID_FP32>
 __global__ void __launch_bounds__(256) slot_readout_kernel(
-    const bf16* __restrict__ hidden, int hsz, const int32_t* __restrict__ slots, const int32_t* __restrict__ nopts,
-    const void* __restrict__ fw, const bf16* __restrict__ letters, int K, float eps, float temp,
-    float* __restrict__ probs, float* __restrict__ logits) {
+    const void* __restrict__ hidden, const bf16* __restrict__ delta, int hsz, const int32_t* __restrict__ slots,
+    const int32_t* __restrict__ nopts, const void* __restrict__ fw, const bf16* __restrict__ letters, int K,
+    float eps, float temp, float* __restrict__ probs, float* __restrict__ logits) {
   const int n = blockIdx.x;
-  const bf16* row = hidden + (int64_t)slots[n] * hsz;
+  const int64_t r = (int64_t)slots[n] * hsz;
+  __shared__ float rowv[READOUT_MAX_H];   // the slot row after the final residual add (bf16 values)
   __shared__ float red[8][17];
   __shared__ float s_inv;
   float ss = 0.f;
   for (int i = threadIdx.x; i < hsz; i += 256) {
-    float x = __bfloat162float(row[i]);
+    float x = HID_FP32 ? static_cast<const float*>(hidden)[r + i] : __bfloat162float(static_cast<const bf16*>(hidden)[r + i]);
+    if (delta) {
+      x += __bfloat162float(delta[r + i]);
+      if (!HID_FP32) x = round_bf16(x);  // the bf16 residual stream rounds the last add
+    }
+    rowv[i] = x;
     ss = fmaf(x, x, ss);
   }
   ss = warp_sum(ss);
@@ -75,7 +83,7 @@ __global__ void __launch_bounds__(256) slot_readout_kernel(
   for (int k = 0; k < 16; ++k) acc[k] = 0.f;
   for (int i = threadIdx.x; i < hsz; i += 256) {
     const float wf = W_FP32 ? static_cast<const float*>(fw)[i] : __bfloat162float(static_cast<const bf16*>(fw)[i]);
-    const float hn = __bfloat162float(row[i]) * inv * (1.0f + wf);
+    const float hn = rowv[i] * inv * (1.0f + wf);
 #pragma unroll
     for (int k = 0; k < 16; ++k)
       if (k < K) acc[k] = fmaf(hn, __bfloat162float(letters[(int64_t)k * hsz + i]), acc[k]);
@@ -146,22 +154,28 @@ extern "C" int fdk_swiglu(const void* gu, int64_t ld_gu, void* out, int64_t toke
   return check_launch("swiglu");
 }
 
-extern "C" int fdk_slot_readout(const void* hidden, int64_t hidden_size, const int32_t* slots, const int32_t* nopts,
-                                int64_t num_slots, const void* final_norm_w, int weight_is_fp32, const void* letters,
-                                int64_t num_letters, float eps, float temperature, float* probs, float* logits,
-                                void* stream) {
+extern "C" int fdk_slot_readout(const void* hidden, int hidden_is_fp32, const void* delta, int64_t hidden_size, const int32_t* slots,
+                                const int32_t* nopts, int64_t num_slots, const void* final_norm_w, int weight_is_fp32,
+                                const void* letters, int64_t num_letters, float eps, float temperature, float* probs,
+                                float* logits, void* stream) {
   if (int st = check_device()) return st;
   if (!hidden || !slots || !nopts || !final_norm_w || !letters || !probs)
     return set_error(FDK_ERR_INVALID_ARGUMENT, "slot_readout: null pointer");
   if (num_letters < 1 || num_letters > 16) return set_error(FDK_ERR_UNSUPPORTED, "slot_readout: 1..16 letters supported");
-  if (hidden_size <= 0 || num_slots < 0 || !(temperature > 0.f)) return set_error(FDK_ERR_INVALID_ARGUMENT, "slot_readout: bad sizes");
+  if (hidden_size <= 0 || hidden_size > READOUT_MAX_H || num_slots < 0 || !(temperature > 0.f))
+    return set_error(FDK_ERR_INVALID_ARGUMENT, "slot_readout: bad sizes (hidden_size <= %d)", READOUT_MAX_H);
   if (num_slots == 0) return FDK_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (weight_is_fp32)
-    slot_readout_kernel<true><<<(unsigned)num_slots, 256, 0, s>>>(static_cast<const bf16*>(hidden), (int)hidden_size, slots, nopts, final_norm_w,
-                                                                  static_cast<const bf16*>(letters), (int)num_letters, eps, temperature, probs, logits);
-  else
-    slot_readout_kernel<false><<<(unsigned)num_slots, 256, 0, s>>>(static_cast<const bf16*>(hidden), (int)hidden_size, slots, nopts, final_norm_w,
-                                                                   static_cast<const bf16*>(letters), (int)num_letters, eps, temperature, probs, logits);
+  auto db = static_cast<const bf16*>(delta);
+  auto lb = static_cast<const bf16*>(letters);
+  const unsigned g = (unsigned)num_slots;
+  const int H = (int)hidden_size, K = (int)num_letters;
+  if (weight_is_fp32) {
+    if (hidden_is_fp32) slot_readout_kernel<true, true><<<g, 256, 0, s>>>(hidden, db, H, slots, nopts, final_norm_w, lb, K, eps, temperature, probs, logits);
+    else slot_readout_kernel<true, false><<<g, 256, 0, s>>>(hidden, db, H, slots, nopts, final_norm_w, lb, K, eps, temperature, probs, logits);
+  } else {
+    if (hidden_is_fp32) slot_readout_kernel<false, true><<<g, 256, 0, s>>>(hidden, db, H, slots, nopts, final_norm_w, lb, K, eps, temperature, probs, logits);
+    else slot_readout_kernel<false, false><<<g, 256, 0, s>>>(hidden, db, H, slots, nopts, final_norm_w, lb, K, eps, temperature, probs, logits);
+  }
   return check_launch("slot_readout");
 }

@@ -8,34 +8,58 @@ namespace fdk {
 // ---------------------------------------------------------------------------------------------
 // Residual add + RMSNorm: one row per 128-thread warp group; each thread keeps its NC 8-wide
 // chunks of the row in registers between the sum-of-squares pass and the scaling pass.
+// RES_FP32 selects the residual stream's storage: bf16 (s rounded to bf16 before the norm reads
+// it, as the eager bf16 model stores it) or float32 (no rounding of the running sum).
 // ---------------------------------------------------------------------------------------------
-template <int NC, bool HAS_RES, bool W_FP32>
+template <bool RES_FP32>
+struct ResIO;
+template <>
+struct ResIO<false> {
+  using T = bf16;
+  static __device__ __forceinline__ void load(const T* p, float (&f)[8]) { unpack8(ldg_stream(p), f); }
+  static __device__ __forceinline__ void store(T* p, const float (&f)[8]) { *reinterpret_cast<uint4*>(p) = pack8(f); }
+  static __device__ __forceinline__ float keep(float x) { return round_bf16(x); }
+};
+template <>
+struct ResIO<true> {
+  using T = float;
+  static __device__ __forceinline__ void load(const T* p, float (&f)[8]) {
+    float4 a = __ldcs(reinterpret_cast<const float4*>(p)), b = __ldcs(reinterpret_cast<const float4*>(p) + 1);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  }
+  static __device__ __forceinline__ void store(T* p, const float (&f)[8]) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(f[0], f[1], f[2], f[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(f[4], f[5], f[6], f[7]);
+  }
+  static __device__ __forceinline__ float keep(float x) { return x; }
+};
+
+template <int NC, bool HAS_RES, bool W_FP32, bool RES_FP32>
 __global__ void __launch_bounds__(128) residual_rmsnorm_kernel(
-    const bf16* __restrict__ x, int64_t ldx, const bf16* __restrict__ res, int64_t ldr,
-    const void* __restrict__ w, bf16* __restrict__ out, int64_t ldo, bf16* __restrict__ res_out,
+    const bf16* __restrict__ x, int64_t ldx, const void* __restrict__ res_, int64_t ldr,
+    const void* __restrict__ w, bf16* __restrict__ out, int64_t ldo, void* __restrict__ res_out_,
     int64_t ldro, int hidden, float eps, float woff) {
+  using IO = ResIO<RES_FP32>;
+  using RT = typename IO::T;
+  const RT* res = static_cast<const RT*>(res_);
+  RT* res_out = static_cast<RT*>(res_out_);
   const int64_t row = blockIdx.x;
   const int nvec = hidden >> 3;
   const bf16* xr = x + row * ldx;
-  const bf16* rr = HAS_RES ? res + row * ldr : nullptr;
   float v[NC][8];
   float ss = 0.f;
 #pragma unroll
   for (int c = 0; c < NC; ++c) {
     const int i = threadIdx.x + c * 128;
     if (i < nvec) {
-      uint4 ux = ldg_stream(xr + i * 8);
-      unpack8(ux, v[c]);
+      unpack8(ldg_stream(xr + i * 8), v[c]);
       if (HAS_RES) {
         float r8[8];
-        uint4 ur = ldg_stream(rr + i * 8);
-        unpack8(ur, r8);
+        IO::load(res + row * ldr + i * 8, r8);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[c][j] = round_bf16(v[c][j] + r8[j]);  // s is stored in bf16
-        if (res_out != nullptr) *reinterpret_cast<uint4*>(res_out + row * ldro + i * 8) = pack8(v[c]);
-      } else if (res_out != nullptr) {
-        *reinterpret_cast<uint4*>(res_out + row * ldro + i * 8) = ux;
+        for (int j = 0; j < 8; ++j) v[c][j] = IO::keep(v[c][j] + r8[j]);
       }
+      if (res_out != nullptr) IO::store(res_out + row * ldro + i * 8, v[c]);
 #pragma unroll
       for (int j = 0; j < 8; ++j) ss = fmaf(v[c][j], v[c][j], ss);
     }
@@ -68,17 +92,25 @@ __global__ void __launch_bounds__(128) residual_rmsnorm_kernel(
   }
 }
 
-template <int NC>
+template <int NC, bool RES_FP32>
 static void launch_rms(bool has_res, bool w32, dim3 grid, cudaStream_t s, const bf16* x, int64_t ldx,
-                       const bf16* r, int64_t ldr, const void* w, bf16* o, int64_t ldo, bf16* ro,
+                       const void* r, int64_t ldr, const void* w, bf16* o, int64_t ldo, void* ro,
                        int64_t ldro, int hidden, float eps, float woff) {
   if (has_res) {
-    if (w32) residual_rmsnorm_kernel<NC, true, true><<<grid, 128, 0, s>>>(x, ldx, r, ldr, w, o, ldo, ro, ldro, hidden, eps, woff);
-    else     residual_rmsnorm_kernel<NC, true, false><<<grid, 128, 0, s>>>(x, ldx, r, ldr, w, o, ldo, ro, ldro, hidden, eps, woff);
+    if (w32) residual_rmsnorm_kernel<NC, true, true, RES_FP32><<<grid, 128, 0, s>>>(x, ldx, r, ldr, w, o, ldo, ro, ldro, hidden, eps, woff);
+    else     residual_rmsnorm_kernel<NC, true, false, RES_FP32><<<grid, 128, 0, s>>>(x, ldx, r, ldr, w, o, ldo, ro, ldro, hidden, eps, woff);
   } else {
-    if (w32) residual_rmsnorm_kernel<NC, false, true><<<grid, 128, 0, s>>>(x, ldx, r, ldr, w, o, ldo, ro, ldro, hidden, eps, woff);
-    else     residual_rmsnorm_kernel<NC, false, false><<<grid, 128, 0, s>>>(x, ldx, r, ldr, w, o, ldo, ro, ldro, hidden, eps, woff);
+    if (w32) residual_rmsnorm_kernel<NC, false, true, RES_FP32><<<grid, 128, 0, s>>>(x, ldx, r, ldr, w, o, ldo, ro, ldro, hidden, eps, woff);
+    else     residual_rmsnorm_kernel<NC, false, false, RES_FP32><<<grid, 128, 0, s>>>(x, ldx, r, ldr, w, o, ldo, ro, ldro, hidden, eps, woff);
   }
+}
+
+template <int NC>
+static void launch_rms_any(bool res32, bool has_res, bool w32, dim3 grid, cudaStream_t s, const bf16* x, int64_t ldx,
+                           const void* r, int64_t ldr, const void* w, bf16* o, int64_t ldo, void* ro,
+                           int64_t ldro, int hidden, float eps, float woff) {
+  if (res32) launch_rms<NC, true>(has_res, w32, grid, s, x, ldx, r, ldr, w, o, ldo, ro, ldro, hidden, eps, woff);
+  else       launch_rms<NC, false>(has_res, w32, grid, s, x, ldx, r, ldr, w, o, ldo, ro, ldro, hidden, eps, woff);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -197,9 +229,9 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
 using namespace fdk;
 
 extern "C" int fdk_residual_rmsnorm(const void* x, int64_t ld_x, const void* residual, int64_t ld_residual,
-                                    const void* weight, int weight_is_fp32, void* out, int64_t ld_out,
-                                    void* residual_out, int64_t ld_residual_out, int64_t rows, int64_t hidden,
-                                    float eps, float weight_offset, void* stream) {
+                                    int residual_is_fp32, const void* weight, int weight_is_fp32, void* out,
+                                    int64_t ld_out, void* residual_out, int64_t ld_residual_out, int64_t rows,
+                                    int64_t hidden, float eps, float weight_offset, void* stream) {
   if (int st = check_device()) return st;
   if (!x || !weight || !out) return set_error(FDK_ERR_INVALID_ARGUMENT, "residual_rmsnorm: null pointer");
   if (rows < 0 || hidden <= 0 || hidden % 8 != 0 || hidden > 8192)
@@ -215,16 +247,14 @@ extern "C" int fdk_residual_rmsnorm(const void* x, int64_t ld_x, const void* res
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int nc = (int)((hidden / 8 + 127) / 128);
   auto xb = static_cast<const bf16*>(x);
-  auto rb = static_cast<const bf16*>(residual);
   auto ob = static_cast<bf16*>(out);
-  auto rob = static_cast<bf16*>(residual_out);
-  bool hr = residual != nullptr, w32 = weight_is_fp32 != 0;
+  const bool hr = residual != nullptr, w32 = weight_is_fp32 != 0, r32 = residual_is_fp32 != 0;
   switch (nc) {
-    case 1: launch_rms<1>(hr, w32, grid, s, xb, ld_x, rb, ld_residual, weight, ob, ld_out, rob, ld_residual_out, (int)hidden, eps, weight_offset); break;
-    case 2: launch_rms<2>(hr, w32, grid, s, xb, ld_x, rb, ld_residual, weight, ob, ld_out, rob, ld_residual_out, (int)hidden, eps, weight_offset); break;
+    case 1: launch_rms_any<1>(r32, hr, w32, grid, s, xb, ld_x, residual, ld_residual, weight, ob, ld_out, residual_out, ld_residual_out, (int)hidden, eps, weight_offset); break;
+    case 2: launch_rms_any<2>(r32, hr, w32, grid, s, xb, ld_x, residual, ld_residual, weight, ob, ld_out, residual_out, ld_residual_out, (int)hidden, eps, weight_offset); break;
     case 3:
-    case 4: launch_rms<4>(hr, w32, grid, s, xb, ld_x, rb, ld_residual, weight, ob, ld_out, rob, ld_residual_out, (int)hidden, eps, weight_offset); break;
-    default: launch_rms<8>(hr, w32, grid, s, xb, ld_x, rb, ld_residual, weight, ob, ld_out, rob, ld_residual_out, (int)hidden, eps, weight_offset); break;
+    case 4: launch_rms_any<4>(r32, hr, w32, grid, s, xb, ld_x, residual, ld_residual, weight, ob, ld_out, residual_out, ld_residual_out, (int)hidden, eps, weight_offset); break;
+    default: launch_rms_any<8>(r32, hr, w32, grid, s, xb, ld_x, residual, ld_residual, weight, ob, ld_out, residual_out, ld_residual_out, (int)hidden, eps, weight_offset); break;
   }
   return check_launch("residual_rmsnorm");
 }

@@ -1,0 +1,282 @@
+"""Decision engine: the whole one-pass decision forward on one B200, over the C ABI.
+
+Mirrors what the reference's ``Engine`` does around ``core(input_ids)`` (src/decider/engine.py:
+77-181): embed -> 24 decoder layers -> final norm at the decision slots -> restricted logits ->
+softmax, with the projections and MLP as cuBLAS GEMMs and every other op a kernel of
+``libfdk.so``.  Differences that make it B200-native:
+
+* requests are packed end to end (varlen ``cu_seqlens``) instead of right-padded to (B, T)
+  buckets: the conv, delta rule and attention kernels restart at every segment boundary, so one
+  forward serves any mix of request lengths without padding work;
+* per-layer projections are fused into one GEMM each (GDN: qkv|z|b|a, attention: q|k|v, MLP:
+  gate|up), the residual add is fused into the following RMSNorm, the attention output gate into
+  the attention epilogue, and the last residual add into the slot readout (only slot rows);
+* fixed shapes (e.g. batch-1 decisions of one length) are captured once into a CUDA graph and
+  replayed, like the reference's bucketed graphs (engine.py:123-149).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from types import SimpleNamespace
+from typing import Optional, Sequence
+
+import numpy as np
+import torch
+
+from . import ops
+from .workloads import LETTER_IDS, ModelConfig, Request, letter_weight
+
+
+@dataclass
+class PackedBatch:
+    """Host-side packed varlen batch (int32 arrays) of ``len(slots)`` requests."""
+    ids: np.ndarray
+    cu_seqlens: np.ndarray
+    positions: np.ndarray
+    slots: np.ndarray        # absolute token row of each request's decision slot
+    nopts: np.ndarray
+    max_seqlen: int
+
+    @property
+    def tokens(self) -> int:
+        return int(self.ids.size)
+
+    @property
+    def num_segments(self) -> int:
+        return int(self.slots.size)
+
+
+def pack(requests: Sequence[Request]) -> PackedBatch:
+    lens = np.array([r.ids.size for r in requests], dtype=np.int64)
+    if (lens < 1).any():
+        raise ValueError("every request needs at least one token")
+    cu = np.zeros(len(requests) + 1, dtype=np.int32)
+    np.cumsum(lens, out=cu[1:])
+    ids = np.concatenate([r.ids for r in requests]).astype(np.int32, copy=False)
+    pos = (np.arange(ids.size, dtype=np.int64) - np.repeat(cu[:-1].astype(np.int64), lens)).astype(np.int32)
+    slots = np.array([c + r.slot for c, r in zip(cu[:-1], requests)], dtype=np.int32)
+    if any(not (0 <= r.slot < r.ids.size) for r in requests):
+        raise ValueError("decision slot outside its request")
+    nopts = np.array([r.nopts for r in requests], dtype=np.int32)
+    return PackedBatch(ids, cu, pos, slots, nopts, int(lens.max()))
+
+
+def plan_batches(lengths: Sequence[int], max_tokens: int) -> list:
+    """Greedy packing of requests (longest first) into batches of at most ``max_tokens`` tokens
+    (a request longer than the budget gets a batch of its own)."""
+    order = sorted(range(len(lengths)), key=lambda i: -lengths[i])
+    batches, cur, cur_t = [], [], 0
+    for i in order:
+        if cur and cur_t + lengths[i] > max_tokens:
+            batches.append(cur)
+            cur, cur_t = [], 0
+        cur.append(i)
+        cur_t += lengths[i]
+    if cur:
+        batches.append(cur)
+    return batches
+
+
+class DecisionEngine:
+    def __init__(self, cfg: ModelConfig, weights: dict, device="cuda", letter_ids=LETTER_IDS,
+                 temperature: float = 1.0, residual_fp32: bool = True):
+        """``residual_fp32`` keeps the residual stream in float32 (the sum of the layer outputs is
+        never rounded); with False it is stored in bf16 like the eager bf16 model."""
+        self.cfg = cfg
+        self.residual_fp32 = bool(residual_fp32)
+        self.dev = torch.device(device)
+        self.temperature = float(temperature)
+        dev = self.dev
+        w = weights
+        bf = torch.bfloat16
+
+        def put(t, dtype=bf):
+            return t.to(device=dev, dtype=dtype).contiguous()
+
+        self.embed = put(w["embed_tokens.weight"])
+        self.final_norm = put(w["norm.weight"])
+        self.letters = put(letter_weight(w, letter_ids))
+        self.inv_freq = ops.rope_inv_freq(cfg.head_dim, cfg.partial_rotary_factor, cfg.rope_theta, dev)
+        self.layers = []
+        for i, kind in enumerate(cfg.layer_types):
+            p = f"layers.{i}."
+            L = SimpleNamespace(kind=kind)
+            L.in_norm = put(w[p + "input_layernorm.weight"])
+            L.post_norm = put(w[p + "post_attention_layernorm.weight"])
+            L.w_gu = put(torch.cat([w[p + "mlp.gate_proj.weight"], w[p + "mlp.up_proj.weight"]]))
+            L.w_down = put(w[p + "mlp.down_proj.weight"])
+            if kind == "linear_attention":
+                la = p + "linear_attn."
+                L.w_in = put(torch.cat([w[la + "in_proj_qkv.weight"], w[la + "in_proj_z.weight"],
+                                        w[la + "in_proj_b.weight"], w[la + "in_proj_a.weight"]]))
+                cw = w[la + "conv1d.weight"]
+                L.conv = put(cw.reshape(cw.shape[0], cw.shape[-1]))
+                L.A_log = put(w[la + "A_log"], torch.float32)
+                L.dt_bias = put(w[la + "dt_bias"], torch.float32)
+                L.gnorm = put(w[la + "norm.weight"])
+                L.w_out = put(w[la + "out_proj.weight"])
+            else:
+                sa = p + "self_attn."
+                L.w_qkv = put(torch.cat([w[sa + "q_proj.weight"], w[sa + "k_proj.weight"], w[sa + "v_proj.weight"]]))
+                L.q_norm = put(w[sa + "q_norm.weight"])
+                L.k_norm = put(w[sa + "k_norm.weight"])
+                L.w_o = put(w[sa + "o_proj.weight"])
+            self.layers.append(L)
+        self._ws: Optional[torch.Tensor] = None
+        self._graphs = {}
+        self.stats = dict(forwards=0, graph_captures=0, graph_replays=0)
+        self.kernel_timer = None  # optional callable(name) -> context manager, set by the bench
+
+    # ------------------------------------------------------------------ workspace
+    def _workspace(self, tokens: int, segments: int) -> torch.Tensor:
+        need = ops.delta_rule_workspace_bytes(tokens, segments, self.cfg.linear_num_value_heads)
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(need, device=self.dev, dtype=torch.uint8)
+        return self._ws
+
+    def reserve(self, tokens: int, segments: int):
+        """Pre-size the delta-rule scratch (call before graph capture)."""
+        self._workspace(tokens, segments)
+
+    # ------------------------------------------------------------------ forward
+    def _timed(self, name):
+        if self.kernel_timer is None:
+            import contextlib
+            return contextlib.nullcontext()
+        return self.kernel_timer(name)
+
+    def _mixer_mlp(self, i: int, x: torch.Tensor, h: torch.Tensor, cu: torch.Tensor, pos: torch.Tensor,
+                   max_seqlen: int, ws: torch.Tensor):
+        """Layer ``i`` given its normalised input ``x`` (bf16) and the residual stream ``h``:
+        token mixer, residual add fused into post_attention_layernorm, SwiGLU MLP.  Updates ``h`` in
+        place to ``h + mixer`` and returns the MLP output (the caller adds it)."""
+        c = self.cfg
+        L = self.layers[i]
+        T = x.shape[0]
+        Hk, Hv = c.linear_num_key_heads, c.linear_num_value_heads
+        Dk, Dv = c.linear_key_head_dim, c.linear_value_head_dim
+        kd, vd = Hk * Dk, Hv * Dv
+        C = 2 * kd + vd
+        hq, hkv, D = c.num_attention_heads, c.num_key_value_heads, c.head_dim
+        if L.kind == "linear_attention":
+            proj = torch.matmul(x, L.w_in.t())                                           # [T, C + vd + 2 Hv]
+            q, k, v = ops.packed_conv_qkv(proj[:, :C].unsqueeze(0), L.conv, kd, vd, Dk, cu)
+            g, beta = ops.gdn_gates(proj[:, C + vd + Hv:C + vd + 2 * Hv], proj[:, C + vd:C + vd + Hv],
+                                    L.A_log, L.dt_bias)
+            with self._timed("delta_rule"):
+                o, _ = ops.chunk_gated_delta_rule(q, k, v, g.unsqueeze(0), beta.unsqueeze(0), cu_seqlens=cu,
+                                                  workspace=ws)
+            on = ops.gated_rmsnorm(o.view(T, Hv, Dv), proj[:, C:C + vd], L.gnorm, c.rms_norm_eps)
+            mix = torch.matmul(on, L.w_out.t())
+        else:
+            proj = torch.matmul(x, L.w_qkv.t())                                          # [T, (2 hq + 2 hkv) D]
+            q, k = ops.attn_qk_norm_rope(proj, L.q_norm, L.k_norm, pos, self.inv_freq, hq, hkv, D, c.rms_norm_eps)
+            v = proj[:, (2 * hq + hkv) * D:].view(T, hkv, D)
+            with self._timed("gqa_attention"):
+                o = ops.gqa_attention_varlen_(q, k, v, cu, max_seqlen, gate=proj[:, D:], gate_interleaved=True)
+            mix = torch.matmul(o.view(T, hq * D), L.w_o.t())
+        x2, _ = ops.residual_rmsnorm(mix, h, L.post_norm, c.rms_norm_eps, residual_out=h)
+        act = ops.swiglu(torch.matmul(x2, L.w_gu.t()), c.intermediate_size)
+        return torch.matmul(act, L.w_down.t())
+
+    @torch.no_grad()
+    def forward_device(self, ids: torch.Tensor, cu: torch.Tensor, pos: torch.Tensor, slots: torch.Tensor,
+                       nopts: torch.Tensor, max_seqlen: int, probs: Optional[torch.Tensor] = None,
+                       logits: Optional[torch.Tensor] = None, trace: Optional[list] = None):
+        """All inputs int32 on the engine's device.  Returns ``(probs, logits)`` float32 ``[S, K]``.
+        ``trace`` (a list, diagnostics only) receives the residual stream after every layer."""
+        c = self.cfg
+        ws = self._workspace(ids.numel(), cu.numel() - 1)
+        self.stats["forwards"] += 1
+        e = ops.embed(ids, self.embed)
+        x, h = ops.residual_rmsnorm(e, None, self.layers[0].in_norm, c.rms_norm_eps,
+                                    residual_fp32=self.residual_fp32)
+        down = None
+        for i in range(len(self.layers)):
+            down = self._mixer_mlp(i, x, h, cu, pos, max_seqlen, ws)
+            if i + 1 < len(self.layers):
+                x, _ = ops.residual_rmsnorm(down, h, self.layers[i + 1].in_norm, c.rms_norm_eps, residual_out=h)
+                if trace is not None:
+                    trace.append(h.clone())
+            elif trace is not None:
+                last = h.float() + down.float()
+                trace.append(last if self.residual_fp32 else last.bfloat16())
+        return ops.slot_readout(h, slots, nopts, self.final_norm, self.letters, c.rms_norm_eps, self.temperature,
+                                probs=probs, logits=logits, delta=down)
+
+    @torch.no_grad()
+    def layer_output(self, i: int, h_in: torch.Tensor, cu: torch.Tensor, pos: torch.Tensor, max_seqlen: int):
+        """Residual stream after layer ``i`` alone, given the stream ``h_in [T, H]`` before it
+        (parity tests feed the oracle's own stream here, so each layer is checked in isolation)."""
+        c = self.cfg
+        h = h_in.to(self.dev, torch.float32 if self.residual_fp32 else torch.bfloat16).contiguous().clone()
+        zero = torch.zeros(h.shape, device=self.dev, dtype=torch.bfloat16)
+        x, _ = ops.residual_rmsnorm(zero, h, self.layers[i].in_norm, c.rms_norm_eps, residual_out=h)
+        down = self._mixer_mlp(i, x, h, cu, pos, max_seqlen, self._workspace(h.shape[0], cu.numel() - 1))
+        return h.float() + down.float()
+
+    # ------------------------------------------------------------------ host API
+    def to_device(self, batch: PackedBatch, pinned: Optional[torch.Tensor] = None):
+        """One pinned host buffer -> one H2D copy; returns device views (ids, cu, pos, slots, nopts)."""
+        parts = [batch.ids, batch.cu_seqlens, batch.positions, batch.slots, batch.nopts]
+        n = sum(p.size for p in parts)
+        if pinned is None or pinned.numel() < n:
+            pinned = torch.empty(n, dtype=torch.int32, pin_memory=True)
+        off = 0
+        host = pinned.numpy()
+        for p in parts:
+            host[off:off + p.size] = p
+            off += p.size
+        dev = pinned[:n].to(self.dev, non_blocking=True)
+        out, off = [], 0
+        for p in parts:
+            out.append(dev[off:off + p.size])
+            off += p.size
+        return out, n * 4
+
+    @torch.no_grad()
+    def score(self, requests: Sequence[Request]) -> np.ndarray:
+        """Public API: decision probabilities ``[N, K]`` (numpy) for host-side requests."""
+        batch = pack(requests)
+        (ids, cu, pos, slots, nopts), _ = self.to_device(batch)
+        probs, _ = self.forward_device(ids, cu, pos, slots, nopts, batch.max_seqlen)
+        return probs.cpu().numpy()
+
+    # ------------------------------------------------------------------ CUDA graphs
+    @torch.no_grad()
+    def capture(self, tokens: int, segments: int, max_seqlen: int):
+        """Capture the forward for a fixed (tokens, segments, max_seqlen) shape; returns a key."""
+        key = (tokens, segments, max_seqlen)
+        if key in self._graphs:
+            return key
+        dev = self.dev
+        st = dict(ids=torch.zeros(tokens, dtype=torch.int32, device=dev),
+                  cu=torch.tensor([0] * segments + [tokens], dtype=torch.int32, device=dev),
+                  pos=torch.zeros(tokens, dtype=torch.int32, device=dev),
+                  slots=torch.zeros(segments, dtype=torch.int32, device=dev),
+                  nopts=torch.ones(segments, dtype=torch.int32, device=dev))
+        self.reserve(tokens, segments)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                self.forward_device(st["ids"], st["cu"], st["pos"], st["slots"], st["nopts"], max_seqlen)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            probs, logits = self.forward_device(st["ids"], st["cu"], st["pos"], st["slots"], st["nopts"], max_seqlen)
+        st.update(graph=graph, probs=probs, logits=logits)
+        self._graphs[key] = st
+        self.stats["graph_captures"] += 1
+        return key
+
+    def replay(self, key, ids=None, cu=None, pos=None, slots=None, nopts=None):
+        """Copy new inputs (device tensors of the captured shapes) and replay; returns probs view."""
+        st = self._graphs[key]
+        for name, t in (("ids", ids), ("cu", cu), ("pos", pos), ("slots", slots), ("nopts", nopts)):
+            if t is not None:
+                st[name].copy_(t, non_blocking=True)
+        st["graph"].replay()
+        self.stats["graph_replays"] += 1
+        return st["probs"]

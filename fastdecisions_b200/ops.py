@@ -51,12 +51,17 @@ def _aligned(*ts):
 # ------------------------------------------------------------------------------------------------
 def residual_rmsnorm(x: torch.Tensor, residual: Optional[torch.Tensor], weight: torch.Tensor,
                      eps: float = 1e-6, weight_offset: float = 1.0, write_residual: bool = True,
-                     out: Optional[torch.Tensor] = None, residual_out: Optional[torch.Tensor] = None):
-    """Returns ``(normed, summed)``: ``summed = bf16(x + residual)`` (x when residual is None),
+                     out: Optional[torch.Tensor] = None, residual_out: Optional[torch.Tensor] = None,
+                     residual_fp32: Optional[bool] = None):
+    """Returns ``(normed, summed)``: ``summed = x + residual`` (x when residual is None), stored in
+    the residual stream's dtype (bf16, rounded, or float32 when ``residual_fp32``), and
     ``normed = bf16(summed * rsqrt(mean(summed^2) + eps) * (weight_offset + w))``."""
     _need_cuda(x, residual, weight)
-    if x.dtype != BF16 or (residual is not None and residual.dtype != BF16):
-        raise ValueError("residual_rmsnorm: inputs must be bf16")
+    if residual_fp32 is None:
+        residual_fp32 = residual is not None and residual.dtype == torch.float32
+    rdt = torch.float32 if residual_fp32 else BF16
+    if x.dtype != BF16 or (residual is not None and residual.dtype != rdt):
+        raise ValueError("residual_rmsnorm: x must be bf16 and the residual bf16 or float32")
     if x.dim() < 1 or x.shape[-1] != weight.numel() or weight.dim() != 1:
         raise ValueError("residual_rmsnorm: weight must be a vector of the hidden size")
     if residual is not None and residual.shape != x.shape:
@@ -76,12 +81,14 @@ def residual_rmsnorm(x: torch.Tensor, residual: Optional[torch.Tensor], weight: 
     if out is None:
         out = torch.empty(x.shape, device=x.device, dtype=BF16)
     if write_residual and residual_out is None:
-        residual_out = torch.empty(x.shape, device=x.device, dtype=BF16)
+        residual_out = torch.empty(x.shape, device=x.device, dtype=rdt)
+    if write_residual and residual_out.dtype != rdt:
+        raise ValueError("residual_rmsnorm: residual_out dtype must match the residual stream")
     o2 = out.reshape(-1, H)
     ro2 = residual_out.reshape(-1, H) if write_residual else None
     with torch.cuda.device(x.device):
         _lib.call("fdk_residual_rmsnorm", x2.data_ptr(), x2.stride(0) if rows > 1 else H,
-                  _ptr(r2), (r2.stride(0) if rows > 1 else H) if r2 is not None else 0,
+                  _ptr(r2), (r2.stride(0) if rows > 1 else H) if r2 is not None else 0, int(residual_fp32),
                   weight.data_ptr(), int(weight.dtype == torch.float32), o2.data_ptr(),
                   o2.stride(0) if rows > 1 else H, _ptr(ro2),
                   (ro2.stride(0) if rows > 1 else H) if ro2 is not None else 0, rows, H,
@@ -448,15 +455,21 @@ def swiglu(gu: torch.Tensor, inter: int, out: Optional[torch.Tensor] = None):
 
 def slot_readout(hidden: torch.Tensor, slots: torch.Tensor, nopts: torch.Tensor, final_norm_w: torch.Tensor,
                  letters: torch.Tensor, eps: float = 1e-6, temperature: float = 1.0,
-                 probs: Optional[torch.Tensor] = None, logits: Optional[torch.Tensor] = None):
-    _need_cuda(hidden, slots, nopts, final_norm_w, letters)
+                 probs: Optional[torch.Tensor] = None, logits: Optional[torch.Tensor] = None,
+                 delta: Optional[torch.Tensor] = None):
+    """Final RMSNorm (1+w) of ``hidden[slots] (+ delta[slots])``, logits over ``letters`` rows and
+    the masked softmax; ``slots`` are absolute token rows, ``nopts`` the options per slot."""
+    _need_cuda(hidden, slots, nopts, final_norm_w, letters, delta)
+    if delta is not None and (delta.shape != hidden.shape or not delta.is_contiguous()):
+        raise ValueError("slot_readout: delta must be a contiguous tensor shaped like hidden")
     N, K = slots.numel(), letters.shape[0]
     if probs is None:
         probs = torch.empty((N, K), device=hidden.device, dtype=torch.float32)
     if logits is None:
         logits = torch.empty((N, K), device=hidden.device, dtype=torch.float32)
     with torch.cuda.device(hidden.device):
-        _lib.call("fdk_slot_readout", hidden.data_ptr(), hidden.shape[-1], slots.data_ptr(), nopts.data_ptr(), N,
+        _lib.call("fdk_slot_readout", hidden.data_ptr(), int(hidden.dtype == torch.float32), _ptr(delta),
+                  hidden.shape[-1], slots.data_ptr(), nopts.data_ptr(), N,
                   final_norm_w.data_ptr(), int(final_norm_w.dtype == torch.float32), letters.data_ptr(), K,
                   float(eps), float(temperature), probs.data_ptr(), logits.data_ptr(), _stream(hidden))
     return probs, logits

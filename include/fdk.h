@@ -49,13 +49,15 @@ const char* fdk_get_last_error_string(void);
  *     s   = bf16(x + residual)                 (s = x when residual == NULL)
  *     out = bf16(s * rsqrt(mean(s^2) + eps) * (weight_offset + w))
  * and also writes s to residual_out when it is non-NULL (the reference kernel omits eps and
- * never writes s).  weight is bf16, or float32 when weight_is_fp32 != 0.  Row strides ld_* are
- * in elements and must keep every row 16-byte aligned; hidden % 8 == 0, hidden <= 8192.
+ * never writes s).  With residual_is_fp32 != 0 the residual stream (residual and residual_out)
+ * is float32 and s is not rounded (s = x + residual in fp32).  x and out are bf16; weight is
+ * bf16, or float32 when weight_is_fp32 != 0.  Row strides ld_* are in elements and must keep
+ * every row 16-byte aligned; hidden % 8 == 0, hidden <= 8192.  residual_out may alias residual.
  */
 int fdk_residual_rmsnorm(const void* x, int64_t ld_x, const void* residual, int64_t ld_residual,
-                         const void* weight, int weight_is_fp32, void* out, int64_t ld_out,
-                         void* residual_out, int64_t ld_residual_out, int64_t rows, int64_t hidden,
-                         float eps, float weight_offset, void* stream);
+                         int residual_is_fp32, const void* weight, int weight_is_fp32, void* out,
+                         int64_t ld_out, void* residual_out, int64_t ld_residual_out, int64_t rows,
+                         int64_t hidden, float eps, float weight_offset, void* stream);
 
 /*
  * Packed depthwise causal conv1d (width kernel_width <= 4, zero left padding) + SiLU that writes
@@ -186,14 +188,18 @@ int fdk_swiglu(const void* gu, int64_t ld_gu, void* out, int64_t tokens, int64_t
  * candidate rows and a masked, temperature-scaled softmax.  Replaces the slot gather,
  * F.linear(h, W_letters) and read_slots/scaled_softmax of src/decider/model.py:18-27 and
  * src/decider/engine.py:48-56 (temperature.py:136-144).
- *     hidden: [tokens, hidden_size] (residual stream after the last layer);
- *     slots, nopts: int32 [num_slots]; letters: [num_letters, hidden_size] bf16;
+ *     hidden: [tokens, hidden_size] residual stream, bf16 (float32 when hidden_is_fp32 != 0);
+ *     delta: NULL or bf16 [tokens, hidden_size] added to it first (the last layer's MLP output,
+ *             [tf]:781; rounded to bf16 when the stream is bf16), so only the slot rows of the
+ *             last residual add are ever formed;
+ *     slots (absolute token index), nopts: int32 [num_slots]; letters: [num_letters, hidden_size];
  *     probs, logits: float32 [num_slots, num_letters] (options >= nopts get p = 0, logit -inf).
  */
-int fdk_slot_readout(const void* hidden, int64_t hidden_size, const int32_t* slots,
-                     const int32_t* nopts, int64_t num_slots, const void* final_norm_w,
-                     int weight_is_fp32, const void* letters, int64_t num_letters, float eps,
-                     float temperature, float* probs, float* logits, void* stream);
+int fdk_slot_readout(const void* hidden, int hidden_is_fp32, const void* delta, int64_t hidden_size,
+                     const int32_t* slots, const int32_t* nopts, int64_t num_slots,
+                     const void* final_norm_w, int weight_is_fp32, const void* letters,
+                     int64_t num_letters, float eps, float temperature, float* probs, float* logits,
+                     void* stream);
 
 #ifdef __cplusplus
 }
