@@ -78,9 +78,24 @@ def poll_device_error() -> int:
     return code.value
 
 
+# kernels each compute entry point launches (used to count device launches in a timed region)
+KERNELS_PER_CALL = {"fdk_chunk_gated_delta_rule_fwd": 3}
+call_counts: dict = {}
+
+
+def launches_since(snapshot: dict) -> int:
+    """Kernel launches issued through the C ABI since ``snapshot`` (a copy of ``call_counts``)."""
+    n = 0
+    for name, c in call_counts.items():
+        if name.startswith("fdk_") and name not in ("fdk_poll_device_error",):
+            n += (c - snapshot.get(name, 0)) * KERNELS_PER_CALL.get(name, 1)
+    return n
+
+
 def call(name: str, *args):
     """Call an fdk_* entry point and map a non-zero status to an exception."""
     lib = load()
+    call_counts[name] = call_counts.get(name, 0) + 1
     st = getattr(lib, name)(*args)
     if st != FDK_OK:
         msg = lib.fdk_get_last_error_string().decode()

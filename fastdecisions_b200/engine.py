@@ -16,6 +16,7 @@ softmax, with the projections and MLP as cuBLAS GEMMs and every other op a kerne
 """
 from __future__ import annotations
 
+import contextlib
 from dataclasses import dataclass
 from types import SimpleNamespace
 from typing import Optional, Sequence
@@ -25,6 +26,9 @@ import torch
 
 from . import ops
 from .workloads import LETTER_IDS, ModelConfig, Request, letter_weight
+
+
+_NULL = contextlib.nullcontext()
 
 
 @dataclass
@@ -124,6 +128,7 @@ class DecisionEngine:
             self.layers.append(L)
         self._ws: Optional[torch.Tensor] = None
         self._graphs = {}
+        self._pinned: Optional[torch.Tensor] = None
         self.stats = dict(forwards=0, graph_captures=0, graph_replays=0)
         self.kernel_timer = None  # optional callable(name) -> context manager, set by the bench
 
@@ -140,9 +145,9 @@ class DecisionEngine:
 
     # ------------------------------------------------------------------ forward
     def _timed(self, name):
+        """Optional per-op CUDA-event timing (the benchmark sets ``kernel_timer``)."""
         if self.kernel_timer is None:
-            import contextlib
-            return contextlib.nullcontext()
+            return _NULL
         return self.kernel_timer(name)
 
     def _mixer_mlp(self, i: int, x: torch.Tensor, h: torch.Tensor, cu: torch.Tensor, pos: torch.Tensor,
@@ -158,26 +163,40 @@ class DecisionEngine:
         kd, vd = Hk * Dk, Hv * Dv
         C = 2 * kd + vd
         hq, hkv, D = c.num_attention_heads, c.num_key_value_heads, c.head_dim
+        tm = self._timed
         if L.kind == "linear_attention":
-            proj = torch.matmul(x, L.w_in.t())                                           # [T, C + vd + 2 Hv]
-            q, k, v = ops.packed_conv_qkv(proj[:, :C].unsqueeze(0), L.conv, kd, vd, Dk, cu)
-            g, beta = ops.gdn_gates(proj[:, C + vd + Hv:C + vd + 2 * Hv], proj[:, C + vd:C + vd + Hv],
-                                    L.A_log, L.dt_bias)
-            with self._timed("delta_rule"):
+            with tm("gemm"):
+                proj = torch.matmul(x, L.w_in.t())                                       # [T, C + vd + 2 Hv]
+            with tm("packed_conv"):
+                q, k, v = ops.packed_conv_qkv(proj[:, :C].unsqueeze(0), L.conv, kd, vd, Dk, cu)
+            with tm("gdn_gates"):
+                g, beta = ops.gdn_gates(proj[:, C + vd + Hv:C + vd + 2 * Hv], proj[:, C + vd:C + vd + Hv],
+                                        L.A_log, L.dt_bias)
+            with tm("delta_rule"):
                 o, _ = ops.chunk_gated_delta_rule(q, k, v, g.unsqueeze(0), beta.unsqueeze(0), cu_seqlens=cu,
                                                   workspace=ws)
-            on = ops.gated_rmsnorm(o.view(T, Hv, Dv), proj[:, C:C + vd], L.gnorm, c.rms_norm_eps)
-            mix = torch.matmul(on, L.w_out.t())
+            with tm("gated_rmsnorm"):
+                on = ops.gated_rmsnorm(o.view(T, Hv, Dv), proj[:, C:C + vd], L.gnorm, c.rms_norm_eps)
+            with tm("gemm"):
+                mix = torch.matmul(on, L.w_out.t())
         else:
-            proj = torch.matmul(x, L.w_qkv.t())                                          # [T, (2 hq + 2 hkv) D]
-            q, k = ops.attn_qk_norm_rope(proj, L.q_norm, L.k_norm, pos, self.inv_freq, hq, hkv, D, c.rms_norm_eps)
+            with tm("gemm"):
+                proj = torch.matmul(x, L.w_qkv.t())                                      # [T, (2 hq + 2 hkv) D]
+            with tm("qk_norm_rope"):
+                q, k = ops.attn_qk_norm_rope(proj, L.q_norm, L.k_norm, pos, self.inv_freq, hq, hkv, D, c.rms_norm_eps)
             v = proj[:, (2 * hq + hkv) * D:].view(T, hkv, D)
-            with self._timed("gqa_attention"):
+            with tm("gqa_attention"):
                 o = ops.gqa_attention_varlen_(q, k, v, cu, max_seqlen, gate=proj[:, D:], gate_interleaved=True)
-            mix = torch.matmul(o.view(T, hq * D), L.w_o.t())
-        x2, _ = ops.residual_rmsnorm(mix, h, L.post_norm, c.rms_norm_eps, residual_out=h)
-        act = ops.swiglu(torch.matmul(x2, L.w_gu.t()), c.intermediate_size)
-        return torch.matmul(act, L.w_down.t())
+            with tm("gemm"):
+                mix = torch.matmul(o.view(T, hq * D), L.w_o.t())
+        with tm("residual_rmsnorm"):
+            x2, _ = ops.residual_rmsnorm(mix, h, L.post_norm, c.rms_norm_eps, residual_out=h)
+        with tm("gemm"):
+            gu = torch.matmul(x2, L.w_gu.t())
+        with tm("swiglu"):
+            act = ops.swiglu(gu, c.intermediate_size)
+        with tm("gemm"):
+            return torch.matmul(act, L.w_down.t())
 
     @torch.no_grad()
     def forward_device(self, ids: torch.Tensor, cu: torch.Tensor, pos: torch.Tensor, slots: torch.Tensor,
@@ -188,21 +207,26 @@ class DecisionEngine:
         c = self.cfg
         ws = self._workspace(ids.numel(), cu.numel() - 1)
         self.stats["forwards"] += 1
-        e = ops.embed(ids, self.embed)
-        x, h = ops.residual_rmsnorm(e, None, self.layers[0].in_norm, c.rms_norm_eps,
-                                    residual_fp32=self.residual_fp32)
+        tm = self._timed
+        with tm("embed"):
+            e = ops.embed(ids, self.embed)
+        with tm("residual_rmsnorm"):
+            x, h = ops.residual_rmsnorm(e, None, self.layers[0].in_norm, c.rms_norm_eps,
+                                        residual_fp32=self.residual_fp32)
         down = None
         for i in range(len(self.layers)):
             down = self._mixer_mlp(i, x, h, cu, pos, max_seqlen, ws)
             if i + 1 < len(self.layers):
-                x, _ = ops.residual_rmsnorm(down, h, self.layers[i + 1].in_norm, c.rms_norm_eps, residual_out=h)
+                with tm("residual_rmsnorm"):
+                    x, _ = ops.residual_rmsnorm(down, h, self.layers[i + 1].in_norm, c.rms_norm_eps, residual_out=h)
                 if trace is not None:
                     trace.append(h.clone())
             elif trace is not None:
                 last = h.float() + down.float()
                 trace.append(last if self.residual_fp32 else last.bfloat16())
-        return ops.slot_readout(h, slots, nopts, self.final_norm, self.letters, c.rms_norm_eps, self.temperature,
-                                probs=probs, logits=logits, delta=down)
+        with tm("slot_readout"):
+            return ops.slot_readout(h, slots, nopts, self.final_norm, self.letters, c.rms_norm_eps, self.temperature,
+                                    probs=probs, logits=logits, delta=down)
 
     @torch.no_grad()
     def layer_output(self, i: int, h_in: torch.Tensor, cu: torch.Tensor, pos: torch.Tensor, max_seqlen: int):
@@ -238,7 +262,10 @@ class DecisionEngine:
     def score(self, requests: Sequence[Request]) -> np.ndarray:
         """Public API: decision probabilities ``[N, K]`` (numpy) for host-side requests."""
         batch = pack(requests)
-        (ids, cu, pos, slots, nopts), _ = self.to_device(batch)
+        n = batch.tokens * 2 + 3 * batch.num_segments + 1
+        if self._pinned is None or self._pinned.numel() < n:
+            self._pinned = torch.empty(max(n, 1 << 16), dtype=torch.int32, pin_memory=True)
+        (ids, cu, pos, slots, nopts), _ = self.to_device(batch, self._pinned)
         probs, _ = self.forward_device(ids, cu, pos, slots, nopts, batch.max_seqlen)
         return probs.cpu().numpy()
 
