@@ -33,7 +33,7 @@ SIGNATURES = {
     "fdk_chunk_gated_delta_rule_fwd": (i32, [vp, vp, i64, vp, i64, vp, vp, vp, i64, i64, i64, i64, i64, f32,
                                              vp, vp, vp, vp, sz, vp]),
     "fdk_gated_rmsnorm": (i32, [vp, vp, i64, vp, i32, vp, i64, i64, i64, f32, vp]),
-    "fdk_attn_qk_norm_rope": (i32, [vp, i64, vp, vp, i32, vp, vp, i32, vp, vp, i64, i64, i64, i64, f32, vp]),
+    "fdk_attn_qk_norm_rope": (i32, [vp, i64, vp, vp, i32, vp, vp, i64, i32, vp, vp, i64, i64, i64, i64, f32, vp]),
     "fdk_gqa_fwd": (i32, [vp, i64, vp, i64, vp, i64, vp, i64, i64, i64, i64, i64, i64, f32, vp, i64, i32, vp, vp]),
     "fdk_poll_device_error": (i32, [C.POINTER(C.c_int)]),
     "fdk_embed": (i32, [vp, vp, i64, i64, vp, i64, vp]),

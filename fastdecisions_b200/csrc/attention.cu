@@ -279,6 +279,7 @@ gqa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     }
   }
   // ------------------------------------------------------------------ teardown
+  __syncwarp();  // lane 0 of the producer / MMA warps rejoins its warp before the aligned barrier
   tc_fence_before();
   __syncthreads();
   if (warp == 9) {

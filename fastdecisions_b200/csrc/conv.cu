@@ -1,20 +1,18 @@
 // Packed depthwise causal conv1d (width <= 4) + SiLU writing q/k/v in [tokens, H, D] layout.
 //
-// Each thread owns 8 consecutive channels (one 16-byte vector) and walks TT consecutive tokens,
-// keeping the last three input rows of its channels in registers: every input byte is read
-// once (plus a 3-row halo per TT-token tile) and every output byte written once, so the kernel
-// runs at HBM speed.  A warp covers 256 contiguous channels, so loads and stores are fully
-// coalesced 512-byte rows.  Segment starts (packed varlen) reset the history to zero.
+// HBM-bound: every input byte is read once (plus a 3-row halo per 64-token tile, an L2 hit) and
+// every output byte written once.  The [B, T, C] projection is read with 16-byte cp.async into
+// shared-memory tiles that carry the causal halo, the 4 taps stay in registers, and q/k/v are
+// written directly in the layout the delta rule reads.  Segment starts (packed varlen) reset the
+// history to zero.
 #include "common.cuh"
 
 namespace fdk {
 
-constexpr int CONV_TT = 16;       // tokens per thread
 constexpr int CONV_THREADS = 128;
 
 __device__ __forceinline__ int64_t segment_start(const int32_t* cu, int nseg, int64_t t) {
-  // largest cu[i] <= t
-  int lo = 0, hi = nseg;  // cu[0] = 0 <= t
+  int lo = 0, hi = nseg;  // largest cu[i] <= t (cu[0] = 0)
   while (lo < hi) {
     int mid = (lo + hi + 1) >> 1;
     if (cu[mid] <= t) lo = mid; else hi = mid - 1;
@@ -23,9 +21,8 @@ __device__ __forceinline__ int64_t segment_start(const int32_t* cu, int nseg, in
 }
 
 __device__ __forceinline__ int64_t next_start(const int32_t* cu, int nseg, int64_t t) {
-  // smallest cu[i] > t (or a sentinel past the end)
+  if (cu[nseg] <= t) return INT64_MAX;  // smallest cu[i] > t
   int lo = 0, hi = nseg;
-  if (cu[nseg] <= t) return INT64_MAX;
   while (lo < hi) {
     int mid = (lo + hi) >> 1;
     if (cu[mid] > t) hi = mid; else lo = mid + 1;
@@ -33,27 +30,59 @@ __device__ __forceinline__ int64_t next_start(const int32_t* cu, int nseg, int64
   return cu[lo];
 }
 
+__device__ __forceinline__ void unpack4(const uint2& u, float (&f)[4]) {
+  float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
+}
+
+// Shared-memory staged variant (the one launched): a CTA owns a 128-channel column block and
+// CONV_TILES_PER_CTA consecutive 64-token tiles.  Tile rows [t0 - 3, t0 + 64) (the 3-row causal
+// halo included) stream into shared memory with cp.async, double-buffered, so the next tile's
+// 16-byte loads are in flight while the current one is convolved.  Thread (cq, rg) computes 4
+// channels x 16 rows with the taps in registers; a warp stores 256 contiguous bytes per row.
+constexpr int CONV_CB = 128;            // channels per CTA
+constexpr int CONV_ROWS = 64;           // tokens per tile
+constexpr int CONV_HALO = 3;
+constexpr int CONV_TILES_PER_CTA = 4;
+constexpr int CONV_SROWS = CONV_ROWS + CONV_HALO;
+
 template <int KW>
-__global__ void __launch_bounds__(CONV_THREADS) packed_conv_silu_kernel(
+__global__ void __launch_bounds__(CONV_THREADS) packed_conv_silu_smem_kernel(
     const bf16* __restrict__ x, int64_t ldx, const bf16* __restrict__ w, int64_t ntok, int64_t period,
     const int32_t* __restrict__ cu, int nseg, int channels, int key_dim, bf16* __restrict__ q,
     bf16* __restrict__ k, bf16* __restrict__ v) {
-  const int cvec = blockIdx.x * CONV_THREADS + threadIdx.x;  // 8-channel group
-  if (cvec * 8 >= channels) return;
-  const int c0 = cvec * 8;
-  const int64_t t0 = (int64_t)blockIdx.y * CONV_TT;
-  if (t0 >= ntok) return;
-  const int64_t t1 = (t0 + CONV_TT < ntok) ? t0 + CONV_TT : ntok;
+  __shared__ __align__(16) bf16 tile[2][CONV_SROWS][CONV_CB];
+  const int tid = threadIdx.x;
+  const int cb0 = blockIdx.x * CONV_CB;
+  const int cq = tid & 31, rg = tid >> 5;   // 4 channels, 16 rows
+  const int c0 = cb0 + cq * 4;
+  const int64_t first = (int64_t)blockIdx.y * CONV_TILES_PER_CTA;
+  const int64_t ntiles = (ntok + CONV_ROWS - 1) / CONV_ROWS;
+  const int64_t last = (first + CONV_TILES_PER_CTA < ntiles) ? first + CONV_TILES_PER_CTA : ntiles;
+  if (first >= last) return;
 
-  // weights of my 8 channels, tap j multiplies x[t - (KW-1) + j]
-  float wr[KW][8];
+  auto issue = [&](int64_t ti, int b) {
+    const int64_t base = ti * CONV_ROWS - CONV_HALO;
+    for (int e = tid; e < CONV_SROWS * (CONV_CB / 8); e += CONV_THREADS) {
+      const int r = e / (CONV_CB / 8), ch = (e % (CONV_CB / 8)) * 8;
+      const int64_t t = base + r;
+      const bool ok = t >= 0 && t < ntok && cb0 + ch < channels;
+      const bf16* src = x + (ok ? t : 0) * ldx + (ok ? cb0 + ch : 0);
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"((uint32_t)__cvta_generic_to_shared(&tile[b][r][ch])),
+                   "l"(src), "r"(ok ? 16 : 0));
+    }
+    asm volatile("cp.async.commit_group;\n" ::);
+  };
+
+  const bool active = c0 < channels;  // the last column block may be partial (threads still sync)
+  float wr[KW][4];
 #pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    const bf16* wc = w + (int64_t)(c0 + c) * KW;
+  for (int c = 0; c < 4; ++c) {
+    const bf16* wc = w + (int64_t)(active ? c0 + c : 0) * KW;
 #pragma unroll
     for (int j = 0; j < KW; ++j) wr[j][c] = __bfloat162float(wc[j]);
   }
-  // destination: q / k / v region of this channel group (groups never straddle regions)
   bf16* dst;
   int64_t ldd;
   int cc;
@@ -61,60 +90,72 @@ __global__ void __launch_bounds__(CONV_THREADS) packed_conv_silu_kernel(
   else if (c0 < 2 * key_dim) { dst = k; ldd = key_dim; cc = c0 - key_dim; }
   else { dst = v; ldd = channels - 2 * key_dim; cc = c0 - 2 * key_dim; }
 
-  int64_t seg0, nxt;
-  if (cu != nullptr) {
-    seg0 = segment_start(cu, nseg, t0);
-    nxt = next_start(cu, nseg, t0);
-  } else {
-    seg0 = (t0 / period) * period;
-    nxt = seg0 + period;
-  }
-  // history rows x[t0-3], x[t0-2], x[t0-1] (zero before the segment start)
-  float hist[3][8];
-#pragma unroll
-  for (int j = 0; j < 3; ++j) {
-    const int64_t t = t0 - 3 + j;
-    if (t >= seg0) unpack8(ldg_stream(x + t * ldx + c0), hist[j]);
-    else {
-#pragma unroll
-      for (int c = 0; c < 8; ++c) hist[j][c] = 0.f;
+  issue(first, 0);
+  for (int64_t ti = first; ti < last; ++ti) {
+    const int b = (int)((ti - first) & 1);
+    if (ti + 1 < last) {
+      issue(ti + 1, b ^ 1);
+      asm volatile("cp.async.wait_group 1;\n" ::);
+    } else {
+      asm volatile("cp.async.wait_group 0;\n" ::);
     }
-  }
-  uint4 raw[CONV_TT];
+    __syncthreads();
+    const int64_t r0 = ti * CONV_ROWS + rg * 16;   // first output token of this thread
+    if (active) {  // predicated, never around a barrier: every thread reaches both __syncthreads
+      int64_t seg0, nxt;
+      if (cu != nullptr) {
+        seg0 = segment_start(cu, nseg, r0);
+        nxt = next_start(cu, nseg, r0);
+      } else {
+        seg0 = (r0 / period) * period;
+        nxt = seg0 + period;
+      }
+      float hist[3][4];
 #pragma unroll
-  for (int i = 0; i < CONV_TT; ++i) {
-    const int64_t t = t0 + i;
-    if (t < t1) raw[i] = ldg_stream(x + t * ldx + c0);
-  }
+      for (int j = 0; j < 3; ++j) {
+        const int64_t t = r0 - 3 + j;
+        const int sr = rg * 16 + j;  // smem row of token t
+        if (t >= seg0) unpack4(*reinterpret_cast<const uint2*>(&tile[b][sr][cq * 4]), hist[j]);
+        else {
 #pragma unroll
-  for (int i = 0; i < CONV_TT; ++i) {
-    const int64_t t = t0 + i;
-    if (t >= t1) break;
-    if (t == nxt) {  // a new segment starts here: forget the history
+          for (int c = 0; c < 4; ++c) hist[j][c] = 0.f;
+        }
+      }
 #pragma unroll
-      for (int j = 0; j < 3; ++j)
+      for (int i = 0; i < 16; ++i) {
+        const int64_t t = r0 + i;
+        if (t < ntok) {
+          if (t == nxt) {
 #pragma unroll
-        for (int c = 0; c < 8; ++c) hist[j][c] = 0.f;
-      if (cu != nullptr) nxt = next_start(cu, nseg, t);
-      else nxt += period;
+            for (int j = 0; j < 3; ++j)
+#pragma unroll
+              for (int c = 0; c < 4; ++c) hist[j][c] = 0.f;
+            nxt = (cu != nullptr) ? next_start(cu, nseg, t) : nxt + period;
+          }
+          float cur[4], y[4];
+          unpack4(*reinterpret_cast<const uint2*>(&tile[b][rg * 16 + CONV_HALO + i][cq * 4]), cur);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float acc = wr[KW - 1][c] * cur[c];
+            if (KW >= 2) acc = fmaf(wr[KW - 2][c], hist[2][c], acc);
+            if (KW >= 3) acc = fmaf(wr[KW - 3][c], hist[1][c], acc);
+            if (KW >= 4) acc = fmaf(wr[KW - 4][c], hist[0][c], acc);
+            y[c] = silu(acc);
+          }
+          uint2 o;
+          o.x = pack_bf16x2(y[0], y[1]);
+          o.y = pack_bf16x2(y[2], y[3]);
+          *reinterpret_cast<uint2*>(dst + t * ldd + cc) = o;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            hist[0][c] = hist[1][c];
+            hist[1][c] = hist[2][c];
+            hist[2][c] = cur[c];
+          }
+        }
+      }
     }
-    float cur[8], y[8];
-    unpack8(raw[i], cur);
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      float acc = wr[KW - 1][c] * cur[c];
-      if (KW >= 2) acc = fmaf(wr[KW - 2][c], hist[2][c], acc);
-      if (KW >= 3) acc = fmaf(wr[KW - 3][c], hist[1][c], acc);
-      if (KW >= 4) acc = fmaf(wr[KW - 4][c], hist[0][c], acc);
-      y[c] = silu(acc);
-    }
-    *reinterpret_cast<uint4*>(dst + t * ldd + cc) = pack8(y);
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      hist[0][c] = hist[1][c];
-      hist[1][c] = hist[2][c];
-      hist[2][c] = cur[c];
-    }
+    __syncthreads();  // buffer b is refilled by the issue() two tiles ahead
   }
 }
 
@@ -139,9 +180,10 @@ extern "C" int fdk_packed_conv_silu(const void* x, int64_t ld_x, const void* wei
   if (cu_seqlens && num_segments < 1) return set_error(FDK_ERR_INVALID_ARGUMENT, "packed_conv: num_segments < 1");
   const int64_t ntok = batch * seqlen;
   if (ntok == 0) return FDK_OK;
-  const int64_t tiles = (ntok + CONV_TT - 1) / CONV_TT;
-  if (tiles > 0x7fffffff) return set_error(FDK_ERR_UNSUPPORTED, "packed_conv: too many tokens");
-  dim3 grid((unsigned)((channels / 8 + CONV_THREADS - 1) / CONV_THREADS), (unsigned)tiles);
+  const int64_t tiles = (ntok + CONV_ROWS - 1) / CONV_ROWS;
+  const int64_t groups = (tiles + CONV_TILES_PER_CTA - 1) / CONV_TILES_PER_CTA;
+  if (groups > 0x7fffffff) return set_error(FDK_ERR_UNSUPPORTED, "packed_conv: too many tokens");
+  dim3 grid((unsigned)((channels + CONV_CB - 1) / CONV_CB), (unsigned)groups);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto xb = static_cast<const bf16*>(x);
   auto wb = static_cast<const bf16*>(weight);
@@ -150,10 +192,10 @@ extern "C" int fdk_packed_conv_silu(const void* x, int64_t ld_x, const void* wei
   auto vb = static_cast<bf16*>(v);
   const int nseg = (int)num_segments;
   switch (kernel_width) {
-    case 4: packed_conv_silu_kernel<4><<<grid, CONV_THREADS, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
-    case 3: packed_conv_silu_kernel<3><<<grid, CONV_THREADS, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
-    case 2: packed_conv_silu_kernel<2><<<grid, CONV_THREADS, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
-    default: packed_conv_silu_kernel<1><<<grid, CONV_THREADS, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
+    case 4: packed_conv_silu_smem_kernel<4><<<grid, CONV_THREADS, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
+    case 3: packed_conv_silu_smem_kernel<3><<<grid, CONV_THREADS, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
+    case 2: packed_conv_silu_smem_kernel<2><<<grid, CONV_THREADS, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
+    default: packed_conv_silu_smem_kernel<1><<<grid, CONV_THREADS, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
   }
   return check_launch("packed_conv_silu");
 }

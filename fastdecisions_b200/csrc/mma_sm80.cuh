@@ -60,11 +60,6 @@ __device__ __forceinline__ void load_b_kn(const __nv_bfloat16* base, int ld, int
   ldsm_x4_t(smem_u32(p), b[0], b[1], b[2], b[3]);
 }
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(smem)), "l"(gmem));
 }

@@ -155,7 +155,7 @@ __global__ void __launch_bounds__(256) gated_rmsnorm_kernel(
 template <int E, bool W_FP32>
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
     const bf16* __restrict__ qkv, int64_t ldq, const void* __restrict__ qw, const void* __restrict__ kw,
-    const int32_t* __restrict__ pos, const float* __restrict__ inv_freq, int rot, bf16* __restrict__ qo,
+    const int32_t* __restrict__ pos, const float* __restrict__ rope, int max_pos, int rot, bf16* __restrict__ qo,
     bf16* __restrict__ ko, int64_t tokens, int hq, int hkv, float eps) {
   constexpr int D = E * 32;
   const int64_t gw = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -194,7 +194,9 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
   // partner lane holding feature f +/- rot/2 (rot/2 is a multiple of E since rot % 8 == 0 and E <= 8)
   const int half = rot >> 1;
   const int lane_off = half / E;
-  const float p = (float)pos[t];
+  int p = pos[t];
+  p = p < 0 ? 0 : (p >= max_pos ? max_pos - 1 : p);   // callers guarantee 0 <= pos < max_pos
+  const float* cs = rope + (int64_t)p * rot;            // cos[0:half] then sin[0:half]
   float y[E];
 #pragma unroll
   for (int j = 0; j < E; ++j) {
@@ -202,10 +204,9 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
     const int src_lane = (f < half) ? lane + lane_off : lane - lane_off;
     float partner = __shfl_sync(0xffffffffu, x[j], src_lane < 0 ? 0 : (src_lane > 31 ? 31 : src_lane));
     if (f < rot) {
-      float sn, cs;
-      sincosf(p * inv_freq[f % half], &sn, &cs);
+      const float c = __ldg(cs + (f % half)), sn = __ldg(cs + half + (f % half));
       const float rotv = (f < half) ? -partner : partner;
-      y[j] = x[j] * cs + rotv * sn;
+      y[j] = x[j] * c + rotv * sn;
     } else {
       y[j] = x[j];
     }
@@ -279,11 +280,12 @@ extern "C" int fdk_gated_rmsnorm(const void* o, const void* z, int64_t ld_z, con
 }
 
 extern "C" int fdk_attn_qk_norm_rope(const void* qkv, int64_t ld_qkv, const void* q_norm_w, const void* k_norm_w,
-                                     int weight_is_fp32, const int32_t* positions, const float* inv_freq, int rot_dim,
+                                     int weight_is_fp32, const int32_t* positions, const float* rope_table,
+                                     int64_t max_pos, int rot_dim,
                                      void* q_out, void* k_out, int64_t tokens, int64_t hq, int64_t hkv, int64_t head_dim,
                                      float eps, void* stream) {
   if (int st = check_device()) return st;
-  if (!qkv || !q_norm_w || !k_norm_w || !positions || !inv_freq || !q_out || !k_out)
+  if (!qkv || !q_norm_w || !k_norm_w || !positions || !rope_table || !q_out || !k_out || max_pos < 1 || max_pos > 0x7fffffff)
     return set_error(FDK_ERR_INVALID_ARGUMENT, "attn_qk_norm_rope: null pointer");
   if (head_dim != 128 && head_dim != 256)
     return set_error(FDK_ERR_UNSUPPORTED, "attn_qk_norm_rope: head_dim=%lld (128 or 256)", (long long)head_dim);
@@ -301,11 +303,11 @@ extern "C" int fdk_attn_qk_norm_rope(const void* qkv, int64_t ld_qkv, const void
   auto qo = static_cast<bf16*>(q_out);
   auto ko = static_cast<bf16*>(k_out);
   if (head_dim == 128) {
-    if (weight_is_fp32) qk_norm_rope_kernel<4, true><<<grid, 256, 0, s>>>(in, ld_qkv, q_norm_w, k_norm_w, positions, inv_freq, rot_dim, qo, ko, tokens, (int)hq, (int)hkv, eps);
-    else qk_norm_rope_kernel<4, false><<<grid, 256, 0, s>>>(in, ld_qkv, q_norm_w, k_norm_w, positions, inv_freq, rot_dim, qo, ko, tokens, (int)hq, (int)hkv, eps);
+    if (weight_is_fp32) qk_norm_rope_kernel<4, true><<<grid, 256, 0, s>>>(in, ld_qkv, q_norm_w, k_norm_w, positions, rope_table, (int)max_pos, rot_dim, qo, ko, tokens, (int)hq, (int)hkv, eps);
+    else qk_norm_rope_kernel<4, false><<<grid, 256, 0, s>>>(in, ld_qkv, q_norm_w, k_norm_w, positions, rope_table, (int)max_pos, rot_dim, qo, ko, tokens, (int)hq, (int)hkv, eps);
   } else {
-    if (weight_is_fp32) qk_norm_rope_kernel<8, true><<<grid, 256, 0, s>>>(in, ld_qkv, q_norm_w, k_norm_w, positions, inv_freq, rot_dim, qo, ko, tokens, (int)hq, (int)hkv, eps);
-    else qk_norm_rope_kernel<8, false><<<grid, 256, 0, s>>>(in, ld_qkv, q_norm_w, k_norm_w, positions, inv_freq, rot_dim, qo, ko, tokens, (int)hq, (int)hkv, eps);
+    if (weight_is_fp32) qk_norm_rope_kernel<8, true><<<grid, 256, 0, s>>>(in, ld_qkv, q_norm_w, k_norm_w, positions, rope_table, (int)max_pos, rot_dim, qo, ko, tokens, (int)hq, (int)hkv, eps);
+    else qk_norm_rope_kernel<8, false><<<grid, 256, 0, s>>>(in, ld_qkv, q_norm_w, k_norm_w, positions, rope_table, (int)max_pos, rot_dim, qo, ko, tokens, (int)hq, (int)hkv, eps);
   }
   return check_launch("attn_qk_norm_rope");
 }

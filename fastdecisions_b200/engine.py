@@ -50,10 +50,15 @@ class PackedBatch:
         return int(self.slots.size)
 
 
+MAX_REQUEST_TOKENS = 32768
+
+
 def pack(requests: Sequence[Request]) -> PackedBatch:
     lens = np.array([r.ids.size for r in requests], dtype=np.int64)
     if (lens < 1).any():
         raise ValueError("every request needs at least one token")
+    if (lens > MAX_REQUEST_TOKENS).any():
+        raise ValueError(f"requests are limited to {MAX_REQUEST_TOKENS} tokens")
     cu = np.zeros(len(requests) + 1, dtype=np.int32)
     np.cumsum(lens, out=cu[1:])
     ids = np.concatenate([r.ids for r in requests]).astype(np.int32, copy=False)
@@ -101,6 +106,8 @@ class DecisionEngine:
         self.final_norm = put(w["norm.weight"])
         self.letters = put(letter_weight(w, letter_ids))
         self.inv_freq = ops.rope_inv_freq(cfg.head_dim, cfg.partial_rotary_factor, cfg.rope_theta, dev)
+        self.max_positions = 32768  # requests up to the model's 32k-token context
+        self.rope = ops.rope_table(self.inv_freq, self.max_positions)
         self.layers = []
         for i, kind in enumerate(cfg.layer_types):
             p = f"layers.{i}."
@@ -183,7 +190,7 @@ class DecisionEngine:
             with tm("gemm"):
                 proj = torch.matmul(x, L.w_qkv.t())                                      # [T, (2 hq + 2 hkv) D]
             with tm("qk_norm_rope"):
-                q, k = ops.attn_qk_norm_rope(proj, L.q_norm, L.k_norm, pos, self.inv_freq, hq, hkv, D, c.rms_norm_eps)
+                q, k = ops.attn_qk_norm_rope(proj, L.q_norm, L.k_norm, pos, self.rope, hq, hkv, D, c.rms_norm_eps)
             v = proj[:, (2 * hq + hkv) * D:].view(T, hkv, D)
             with tm("gqa_attention"):
                 o = ops.gqa_attention_varlen_(q, k, v, cu, max_seqlen, gate=proj[:, D:], gate_interleaved=True)

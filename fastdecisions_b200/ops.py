@@ -333,19 +333,30 @@ def rope_inv_freq(head_dim: int, partial_rotary_factor: float = 0.25, theta: flo
     return inv.to(device)
 
 
+def rope_table(inv_freq: torch.Tensor, max_pos: int) -> torch.Tensor:
+    """``[max_pos, rot_dim]`` float32: cos(p * inv_freq) then sin(p * inv_freq) per position,
+    computed as transformers does (fp32 angle ``p * inv_freq``, then cos / sin; [tf]:139-155)."""
+    pos = torch.arange(max_pos, device=inv_freq.device, dtype=torch.float32)
+    ang = pos[:, None] * inv_freq.float()[None, :]
+    return torch.cat([ang.cos(), ang.sin()], dim=1).contiguous()
+
+
 def attn_qk_norm_rope(qkv: torch.Tensor, q_norm_w: torch.Tensor, k_norm_w: torch.Tensor,
-                      positions: torch.Tensor, inv_freq: torch.Tensor, hq: int, hkv: int, head_dim: int,
+                      positions: torch.Tensor, rope: torch.Tensor, hq: int, hkv: int, head_dim: int,
                       eps: float = 1e-6):
-    """``qkv [T, >= (2*hq + hkv)*D]`` (q_proj then k_proj columns) -> ``q [T, hq, D]``, ``k [T, hkv, D]``."""
-    _need_cuda(qkv, q_norm_w, k_norm_w, positions, inv_freq)
+    """``qkv [T, >= (2*hq + hkv)*D]`` (q_proj then k_proj columns) -> ``q [T, hq, D]``, ``k [T, hkv, D]``.
+    ``rope`` is the ``rope_table`` ([max_pos, rot_dim]); positions must be < max_pos."""
+    _need_cuda(qkv, q_norm_w, k_norm_w, positions, rope)
     T = qkv.shape[0]
-    rot = 2 * inv_freq.numel()
+    if rope.dim() != 2 or rope.dtype != torch.float32 or not rope.is_contiguous():
+        raise ValueError("attn_qk_norm_rope: rope must be a contiguous float32 [max_pos, rot_dim] table")
+    rot = rope.shape[1]
     q = torch.empty((T, hq, head_dim), device=qkv.device, dtype=BF16)
     k = torch.empty((T, hkv, head_dim), device=qkv.device, dtype=BF16)
     with torch.cuda.device(qkv.device):
         _lib.call("fdk_attn_qk_norm_rope", qkv.data_ptr(), qkv.stride(0) if T > 1 else qkv.shape[1],
                   q_norm_w.data_ptr(), k_norm_w.data_ptr(), int(q_norm_w.dtype == torch.float32),
-                  positions.data_ptr(), inv_freq.data_ptr(), rot, q.data_ptr(), k.data_ptr(), T, hq, hkv,
+                  positions.data_ptr(), rope.data_ptr(), rope.shape[0], rot, q.data_ptr(), k.data_ptr(), T, hq, hkv,
                   head_dim, float(eps), _stream(qkv))
     return q, k
 

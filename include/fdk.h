@@ -136,15 +136,17 @@ int fdk_gated_rmsnorm(const void* o, const void* z, int64_t ld_z, const void* we
  * experiments/native_gqa/bench_native_gqa_model.py:43-53).
  *     qkv: [tokens, ld_qkv] projection output laid out as q_proj ([hq, 2, head_dim]: query then
  *          output gate per head) followed by k_proj [hkv, head_dim] (v_proj after it is untouched)
- *     positions: int32 [tokens] (position within the request); inv_freq: float32 [rot_dim/2]
+ *     positions: int32 [tokens] (position within the request, 0 <= pos < max_pos);
+ *     rope_table: float32 [max_pos, rot_dim]: row p holds cos(p * inv_freq[i]) for i < rot_dim/2
+ *                 then sin(p * inv_freq[i]) ([tf]:139-155 computes the same table in float32);
  *     q_out: [tokens, hq, head_dim], k_out: [tokens, hkv, head_dim] contiguous.
  * Supports head_dim == 128 or 256 and rot_dim <= head_dim, rot_dim % 8 == 0.
  */
 int fdk_attn_qk_norm_rope(const void* qkv, int64_t ld_qkv, const void* q_norm_w,
                           const void* k_norm_w, int weight_is_fp32, const int32_t* positions,
-                          const float* inv_freq, int rot_dim, void* q_out, void* k_out,
-                          int64_t tokens, int64_t hq, int64_t hkv, int64_t head_dim, float eps,
-                          void* stream);
+                          const float* rope_table, int64_t max_pos, int rot_dim, void* q_out,
+                          void* k_out, int64_t tokens, int64_t hq, int64_t hkv, int64_t head_dim,
+                          float eps, void* stream);
 
 /*
  * Native GQA causal attention, tcgen05 tensor cores with TMEM accumulators fed by TMA.

@@ -206,7 +206,7 @@ def test_attn_qk_norm_rope(D):
     kw = (0.1 * torch.randn(D, generator=g)).bfloat16()
     pos = torch.cat([torch.arange(20), torch.arange(25)]).int()
     inv = ops.rope_inv_freq(D)
-    q, k = ops.attn_qk_norm_rope(dev(qkv), dev(qw), dev(kw), dev(pos), dev(inv), hq, hkv, D)
+    q, k = ops.attn_qk_norm_rope(dev(qkv), dev(qw), dev(kw), dev(pos), ops.rope_table(dev(inv), 64), hq, hkv, D)
     qg = qkv[:, :2 * hq * D].reshape(T, hq, 2 * D)
     qr = O.rmsnorm_offset(qg[..., :D], qw)
     kr = O.rmsnorm_offset(qkv[:, 2 * hq * D:2 * hq * D + hkv * D].reshape(T, hkv, D), kw)
