@@ -643,3 +643,69 @@ extern "C" int fdk_chunk_gated_delta_rule_fwd(const void* q, const void* k, int6
     return launch_recur<2>(nseg, (int)heads, s, cu_seqlens, table, tiles, initial_state, o, final_state);
   return launch_recur<4>(nseg, (int)heads, s, cu_seqlens, table, tiles, initial_state, o, final_state);
 }
+
+// ---------------------------------------------------------------------------------------------
+// Allocation-free variant: the scratch is a file-scope device array instead of a caller-owned
+// workspace.  For callers that reach this library only through the C ABI and own no device
+// allocator (a cgo / JNI / ctypes host without a CUDA framework), or that must not call
+// cudaMalloc / cudaFree on their request path (those calls synchronise the device).
+// ---------------------------------------------------------------------------------------------
+#include <mutex>
+
+namespace fdk {
+
+// 32 MiB: enough for one 1536-token request with 16 heads (config 4).  Every GPU that loads this
+// library holds the array until the process exits.
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;
+static __device__ __align__(256) uint8_t g_delta_noalloc_scratch[kNoAllocScratchBytes];
+
+// Host code cannot pass the array's symbol to a kernel (it names a host-side stand-in), so the
+// device address is looked up once per device, with that device current, and cached.
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[64];
+
+static int noalloc_scratch(void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return set_error(FDK_ERR_DEVICE, "chunk_gated_delta_rule_fwd_noalloc: no usable current device");
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_delta_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      return set_error(FDK_ERR_DEVICE, "chunk_gated_delta_rule_fwd_noalloc: cudaGetSymbolAddress failed on device %d: %s",
+                       dev, cudaGetErrorString(e));
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return FDK_OK;
+}
+
+}  // namespace fdk
+
+extern "C" int fdk_chunk_gated_delta_rule_fwd_noalloc(const void* q, const void* k, int64_t ld_qk, const void* v,
+                                                      int64_t ld_v, const float* g, const void* beta,
+                                                      const int32_t* cu_seqlens, int64_t num_segments, int64_t tokens,
+                                                      int64_t heads, int64_t dk, int64_t dv, float scale,
+                                                      const float* initial_state, void* out, float* final_state,
+                                                      void* stream) {
+  using namespace fdk;
+  if (int st = check_device()) return st;
+  const size_t need = fdk_chunk_gated_delta_rule_workspace_size(tokens, num_segments, heads, dk, dv);
+  if (need == 0)
+    return set_error(FDK_ERR_UNSUPPORTED, "chunk_gated_delta_rule_fwd_noalloc: unsupported sizes (dk = dv = 128, "
+                     "num_segments >= 1, heads >= 1, tokens >= 0)");
+  if (need > kNoAllocScratchBytes)
+    return set_error(FDK_ERR_UNSUPPORTED,
+                     "chunk_gated_delta_rule_fwd_noalloc: this call needs %zu bytes of scratch but the built-in scratch "
+                     "holds %zu (32 MiB); pass a workspace to fdk_chunk_gated_delta_rule_fwd instead",
+                     need, kNoAllocScratchBytes);
+  void* ws = nullptr;
+  if (int st = noalloc_scratch(&ws)) return st;
+  return fdk_chunk_gated_delta_rule_fwd(q, k, ld_qk, v, ld_v, g, beta, cu_seqlens, num_segments, tokens, heads, dk, dv,
+                                        scale, initial_state, out, final_state, ws, kNoAllocScratchBytes, stream);
+}

@@ -120,6 +120,31 @@ int fdk_chunk_gated_delta_rule_fwd(const void* q, const void* k, int64_t ld_qk, 
                                    void* stream);
 
 /*
+ * Allocation-free form of fdk_chunk_gated_delta_rule_fwd (same arguments and results, no
+ * workspace).  No counterpart in the reference.  It is for callers that cannot allocate device
+ * memory: programs that reach this library only through its C ABI and own no device allocator
+ * (a cgo, JNI or ctypes host without a CUDA framework), and servers that must not call
+ * cudaMalloc / cudaFree on the request path because those calls synchronise the device.
+ *   - Scratch: a 32 MiB array inside the library (one per GPU that loads it, held until the
+ *     process exits).  A call whose fdk_chunk_gated_delta_rule_workspace_size(...) exceeds
+ *     32 MiB is rejected with FDK_ERR_UNSUPPORTED before anything is launched (one 1536-token
+ *     request with 16 heads needs about 29.5 MiB).
+ *   - The first call on a device looks up the array's device address there (with that device
+ *     current) and caches it; make that first call before any stream capture.
+ *   - Nothing in the scratch has to start at zero: each call rebuilds its chunk table and every
+ *     tile it reads.  All calls on a device share the one array and it keeps the last call's
+ *     contents, so calls that overlap on the GPU (concurrent streams) race; serialise them.
+ *   - It calls no cudaMalloc, cudaFree or allocating library routine.
+ */
+int fdk_chunk_gated_delta_rule_fwd_noalloc(const void* q, const void* k, int64_t ld_qk,
+                                           const void* v, int64_t ld_v, const float* g,
+                                           const void* beta, const int32_t* cu_seqlens,
+                                           int64_t num_segments, int64_t tokens, int64_t heads,
+                                           int64_t dk, int64_t dv, float scale,
+                                           const float* initial_state, void* out,
+                                           float* final_state, void* stream);
+
+/*
  * Gated RMSNorm of the GDN output, per head row of width dv:
  *     out = bf16(w * (o * rsqrt(mean(o^2) + eps)) * silu(z))
  * Replaces Qwen3_5RMSNormGated / fla FusedRMSNormGated ([tf]:175-190, call site [tf]:526-529).
