@@ -378,6 +378,9 @@ extern "C" int fdk_poll_device_error(int* code) {
     int zero = 0;
     cudaMemcpyToSymbol(fdk::attn::g_device_error, &zero, sizeof(int));
   }
+  const int d = fdk::delta_take_device_error();
+  if (d < 0) return set_error(FDK_ERR_DEVICE, "poll_device_error: cannot read the device error word");
+  h |= d << 1;
   if (code) *code = h;
   return FDK_OK;
 }

@@ -19,6 +19,8 @@ int check_launch(const char* what);
 int check_device();
 // Number of SMs of the current device (cached per device).
 int sm_count();
+// Reads and clears the delta-rule recurrence's device error word (set when a bounded wait ran out).
+int delta_take_device_error();
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

@@ -17,8 +17,12 @@
 //      An accumulator tile of one product is the A operand of the next (bf16-packed in
 //      registers), so the state never round-trips through shared memory; the chunk tiles stream
 //      in with cp.async, double-buffered, into XOR-swizzled (bank-conflict-free) shared memory.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 #include "mma_sm80.cuh"
+#include "sm100.cuh"
 
 namespace fdk {
 
@@ -361,225 +365,357 @@ __global__ void __launch_bounds__(PREP_THREADS, 2) delta_prep_kernel(
 }
 
 // ------------------------------------------------------------------------------------- recurrence
-struct RecurStage {
-  __nv_bfloat16 w[DR_C * DR_D];    // swizzled [tok][dk]
-  __nv_bfloat16 qg[DR_C * DR_D];   // swizzled [tok][dk]
-  __nv_bfloat16 kg[DR_C * DR_D];   // swizzled [tok][dk]
-  __nv_bfloat16 a[DR_C * DR_C];    // swizzled [tok][tok']
-  float gamma[4];                  // gamma = e^G_last (+ padding of the 16-byte copy)
+// tcgen05 recurrence: one CTA per (segment, head), sequential over the segment's chunks.
+//   TMEM (256 columns of fp32; lane = dv row): S^T [0,128), vn [128,192), o^T [192,256).
+//   Per chunk c, with W, Qg, Kg, Aqk of chunk c in a 2-stage TMA ring (128-byte swizzle):
+//     state warps : o^T of chunk c-1 -> out; S^T -> bf16 A tile in SMEM; S^T *= gamma_c in TMEM
+//     MMA thread  : vn  = S^T W^T            (M128 N64  K128)
+//                   o^T = S^T Qg^T           (M128 N64  K128)
+//     state warps : v_new^T = U^T - vn -> bf16 A tile in SMEM
+//     MMA thread  : S^T += v_new^T Kg        (M128 N128 K64; Kg is MN-major)
+//                   o^T += v_new^T Aqk^T     (M128 N64  K64)
+//   Warps: 0 TMA producer, 1 TMEM allocator + single-thread MMA issuer, 2-5 state warps (one
+//   thread per dv row = TMEM lane).  Every mbarrier wait is bounded; a wait that runs out sets the
+//   device error word and the CTA drains its copies and MMAs, frees TMEM and returns.
+namespace drtc {
+using namespace sm100;
+
+constexpr uint32_t KM_HALF = 64 * 128;  // [64 rows][128 B] swizzled block (one TMA box)
+constexpr uint32_t ST_W = 0, ST_QG = 2 * KM_HALF, ST_KG = 4 * KM_HALF, ST_A = 6 * KM_HALF, ST_BYTES = 7 * KM_HALF;
+constexpr uint32_t OFF_SA = 2 * ST_BYTES;            // S^T bf16 A tile: [2 dk halves][128 dv][128 B]
+constexpr uint32_t OFF_VA = OFF_SA + 2 * 128 * 128;  // v_new^T bf16 A tile: [128 dv][128 B]
+constexpr uint32_t OFF_OST = OFF_VA + 128 * 128;     // o staging: per state warp [64 tok][32 dv] bf16
+constexpr uint32_t OFF_BAR = OFF_OST + 4 * 64 * 32 * 2;
+enum { B_FULL0 = 0, B_FULL1, B_EMPTY0, B_EMPTY1, B_SA, B_VN, B_VNEW, B_SDONE, B_DRAIN, NBAR };
+constexpr uint32_t SMEM_BYTES = OFF_BAR + 8 * NBAR + 16 + 1024;
+constexpr int THREADS = 192;
+constexpr uint32_t TM_S = 0, TM_VN = 128, TM_O = 192, TM_COLS = 256;
+constexpr long long DRAIN_BUDGET = 2000000000LL;
+
+__device__ int g_recur_error = 0;
+
+struct RParams {
+  const int32_t* cu;
+  const int32_t* table;
+  int heads;
+  const uint8_t* tiles;  // workspace tiles (U^T rows and gamma are read from here directly)
+  const float* init_state;
+  bf16* out;
+  float* final_state;
 };
 
-template <int WARPS>
-struct RecurSmem {
-  RecurStage st[2];
-  __nv_bfloat16 o[WARPS][DR_C][16];  // per-warp output staging [tok][16 dv]
-};
-
-__device__ __forceinline__ void recur_prefetch(RecurStage& s, const uint8_t* tile, int tid, int nthreads) {
-  const __nv_bfloat16* W = reinterpret_cast<const __nv_bfloat16*>(tile + OFF_W);
-  const __nv_bfloat16* Qg = reinterpret_cast<const __nv_bfloat16*>(tile + OFF_QG);
-  const __nv_bfloat16* Kg = reinterpret_cast<const __nv_bfloat16*>(tile + OFF_KG);
-  const __nv_bfloat16* A = reinterpret_cast<const __nv_bfloat16*>(tile + OFF_A);
-  for (int e = tid; e < DR_C * 16; e += nthreads) {
-    const int r = e >> 4, c = (e & 15) << 3;
-    cp_async16(&s.w[swz<DR_D>(r, c)], W + r * DR_D + c);
-    cp_async16(&s.qg[swz<DR_D>(r, c)], Qg + r * DR_D + c);
-    cp_async16(&s.kg[swz<DR_D>(r, c)], Kg + r * DR_D + c);
-  }
-  for (int e = tid; e < DR_C * 8; e += nthreads) {
-    const int r = e >> 3, c = (e & 7) << 3;
-    cp_async16(&s.a[swz<DR_C>(r, c)], A + r * DR_C + c);
-  }
-  if (tid == 0) cp_async16(s.gamma, tile + OFF_GAMMA);
-  cp_async_commit();
+// byte offset of 16-byte chunk `c16` of row `r` in a [c16 / 8][rows][128 B] 128-byte-swizzled tile
+__device__ __forceinline__ uint32_t sw128_off(int r, int c16, int rows) {
+  return (uint32_t)(c16 >> 3) * (uint32_t)(rows * 128) + (uint32_t)r * 128u + ((uint32_t)((c16 & 7) ^ (r & 7)) << 4);
 }
 
-// U^T values of this thread for one chunk: rows dv (g, g+8), token pairs (8 nt + 2t, +1)
-__device__ __forceinline__ void load_ut(const uint8_t* tile, int dv0, int gq, int tq, uint32_t (&u)[8][2]) {
-  const __nv_bfloat16* Ut = reinterpret_cast<const __nv_bfloat16*>(tile + OFF_UT);
-#pragma unroll
-  for (int nt = 0; nt < 8; ++nt) {
-    u[nt][0] = __ldg(reinterpret_cast<const unsigned int*>(Ut + (dv0 + gq) * DR_C + nt * 8 + 2 * tq));
-    u[nt][1] = __ldg(reinterpret_cast<const unsigned int*>(Ut + (dv0 + gq + 8) * DR_C + nt * 8 + 2 * tq));
-  }
+// warp-uniform bounded wait: every lane polls, the warp proceeds only if all lanes saw the phase
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  const bool ok = mbar_wait(bar, parity, abort_flag);
+  return __all_sync(0xffffffffu, ok ? 1 : 0) != 0;
 }
 
-template <int WARPS>
-__global__ void __launch_bounds__(WARPS * 32) delta_recur_kernel(
-    const int32_t* __restrict__ cu, int nseg, const int32_t* __restrict__ table, int heads,
-    const uint8_t* __restrict__ tiles, const float* __restrict__ init_state, bf16* __restrict__ out,
-    float* __restrict__ final_state) {
-  extern __shared__ __align__(128) uint8_t smem_raw[];
-  RecurSmem<WARPS>& sm = *reinterpret_cast<RecurSmem<WARPS>*>(smem_raw);
-  constexpr int NT = WARPS * 32;
-  const int s = blockIdx.x, h = blockIdx.y;
+__global__ void __launch_bounds__(THREADS, 1)
+delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_constant__ CUtensorMap mqg,
+                      const __grid_constant__ CUtensorMap mkg, const __grid_constant__ CUtensorMap ma,
+                      const RParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t bar0 = base + OFF_BAR;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + OFF_BAR + 8 * NBAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_BAR + 8 * NBAR + 4);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int gq = lane >> 2, tq = lane & 3;
-  const int dv0 = (blockIdx.z * WARPS + warp) * 16;  // this warp's 16 dv rows
-  const int c0 = table[s], nch = table[s + 1] - c0;
-  const int seg_t0 = cu[s], seg_len = cu[s + 1] - cu[s];
-  const size_t hstride = (size_t)heads * CH_BYTES;
+  const int s = blockIdx.x, h = blockIdx.y, H = p.heads;
+  const int c0 = p.table[s], nch = p.table[s + 1] - c0;
+  const int seg_t0 = p.cu[s], seg_len = p.cu[s + 1] - p.cu[s];
 
-  // S^T [16 dv x 128 dk] as 16 accumulator tiles (rows dv0 + g (+8), cols 8 nt + 2t (+1))
-  float st[16][4];
-#pragma unroll
-  for (int nt = 0; nt < 16; ++nt)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float val = 0.f;
-      if (init_state) {
-        const int dv = dv0 + gq + (j >> 1) * 8, dk = nt * 8 + 2 * tq + (j & 1);
-        val = init_state[(((int64_t)s * heads + h) * DR_D + dk) * DR_D + dv];
-      }
-      st[nt][j] = val;
-    }
-  uint32_t ut[8][2];
-  if (nch > 0) {
-    const uint8_t* tile0 = tiles + ((size_t)c0 * heads + h) * CH_BYTES;
-    recur_prefetch(sm.st[0], tile0, tid, NT);
-    load_ut(tile0, dv0, gq, tq, ut);
+  if (tid == 0) {
+    for (int i = 0; i < NBAR; ++i) mbar_init(bar0 + 8 * i, (i == B_SA || i == B_VNEW) ? 128u : 1u);
+    *abort_flag = 0;
+    fence_mbar_init();
   }
-  for (int c = 0; c < nch; ++c) {
-    const int buf = c & 1;
-    const uint8_t* tile = tiles + ((size_t)(c0 + c) * heads + h) * CH_BYTES;
-    cp_async_wait<0>();
-    __syncthreads();
-    uint32_t ut_next[8][2];
-    if (c + 1 < nch) {
-      recur_prefetch(sm.st[buf ^ 1], tile + hstride, tid, NT);
-      load_ut(tile + hstride, dv0, gq, tq, ut_next);
-    }
-    const RecurStage& S = sm.st[buf];
-    // S^T as bf16 A fragments (8 k-steps over dk)
-    uint32_t sa[8][4];
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      sa[kk][0] = pack_bf16x2(st[2 * kk][0], st[2 * kk][1]);
-      sa[kk][1] = pack_bf16x2(st[2 * kk][2], st[2 * kk][3]);
-      sa[kk][2] = pack_bf16x2(st[2 * kk + 1][0], st[2 * kk + 1][1]);
-      sa[kk][3] = pack_bf16x2(st[2 * kk + 1][2], st[2 * kk + 1][3]);
-    }
-    // 1. v_new^T = U^T - S^T W^T      [16 dv x 64 tok]
-    float vn[8][4];
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) vn[nt][j] = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk)
-#pragma unroll
-      for (int nt = 0; nt < 8; nt += 2) {
-        uint32_t b[4];
-        ldb_nk_sw<DR_D>(S.w, nt * 8, kk * 16, b);
-        mma_bf16_16816(vn[nt], sa[kk], b[0], b[1]);
-        mma_bf16_16816(vn[nt + 1], sa[kk], b[2], b[3]);
-      }
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      const float2 u0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ut[nt][0]));
-      const float2 u1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ut[nt][1]));
-      vn[nt][0] = u0.x - vn[nt][0];
-      vn[nt][1] = u0.y - vn[nt][1];
-      vn[nt][2] = u1.x - vn[nt][2];
-      vn[nt][3] = u1.y - vn[nt][3];
-    }
-    uint32_t va[4][4];  // v_new^T as A fragments (4 k-steps over tokens)
-#pragma unroll
-    for (int kt = 0; kt < 4; ++kt) {
-      va[kt][0] = pack_bf16x2(vn[2 * kt][0], vn[2 * kt][1]);
-      va[kt][1] = pack_bf16x2(vn[2 * kt][2], vn[2 * kt][3]);
-      va[kt][2] = pack_bf16x2(vn[2 * kt + 1][0], vn[2 * kt + 1][1]);
-      va[kt][3] = pack_bf16x2(vn[2 * kt + 1][2], vn[2 * kt + 1][3]);
-    }
-    // 2. o^T = S^T Qg^T + v_new^T Aqk^T   [16 dv x 64 tok]  (old state)
-    float ot[8][4];
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) ot[nt][j] = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk)
-#pragma unroll
-      for (int nt = 0; nt < 8; nt += 2) {
-        uint32_t b[4];
-        ldb_nk_sw<DR_D>(S.qg, nt * 8, kk * 16, b);
-        mma_bf16_16816(ot[nt], sa[kk], b[0], b[1]);
-        mma_bf16_16816(ot[nt + 1], sa[kk], b[2], b[3]);
-      }
-#pragma unroll
-    for (int kt = 0; kt < 4; ++kt)
-#pragma unroll
-      for (int nt = 0; nt < 8; nt += 2) {
-        uint32_t b[4];
-        ldb_nk_sw<DR_C>(S.a, nt * 8, kt * 16, b);
-        mma_bf16_16816(ot[nt], va[kt], b[0], b[1]);
-        mma_bf16_16816(ot[nt + 1], va[kt], b[2], b[3]);
-      }
-    // 3. S^T = gamma S^T + v_new^T Kg     [16 dv x 128 dk]
-    const float gm = S.gamma[0];
-#pragma unroll
-    for (int nt = 0; nt < 16; ++nt)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) st[nt][j] *= gm;
-#pragma unroll
-    for (int kt = 0; kt < 4; ++kt)
-#pragma unroll
-      for (int nt = 0; nt < 16; nt += 2) {
-        uint32_t b[4];
-        ldb_kn_sw<DR_D>(S.kg, nt * 8, kt * 16, b);
-        mma_bf16_16816(st[nt], va[kt], b[0], b[1]);
-        mma_bf16_16816(st[nt + 1], va[kt], b[2], b[3]);
-      }
-    // output: stage o^T as [tok][16 dv] and write 32-byte row pieces
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      const int tk = nt * 8 + 2 * tq;
-      sm.o[warp][tk][gq] = __float2bfloat16_rn(ot[nt][0]);
-      sm.o[warp][tk + 1][gq] = __float2bfloat16_rn(ot[nt][1]);
-      sm.o[warp][tk][gq + 8] = __float2bfloat16_rn(ot[nt][2]);
-      sm.o[warp][tk + 1][gq + 8] = __float2bfloat16_rn(ot[nt][3]);
-    }
-    __syncwarp();
-    const int tok0 = seg_t0 + c * DR_C;
-    const int len = min(DR_C, seg_len - c * DR_C);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int e = lane + i * 32;  // 128 pieces of 16 B: row e/2, half e%2
-      const int r = e >> 1, half = e & 1;
-      if (r < len)
-        *reinterpret_cast<uint4*>(out + ((int64_t)(tok0 + r) * heads + h) * DR_D + dv0 + half * 8) =
-            *reinterpret_cast<const uint4*>(&sm.o[warp][r][half * 8]);
-    }
-    if (c + 1 < nch) {
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) { ut[nt][0] = ut_next[nt][0]; ut[nt][1] = ut_next[nt][1]; }
-    }
-    __syncthreads();  // stage buf is refilled by the prefetch two chunks ahead; o staging reused
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), TM_COLS);
+    tmem_relinquish();
   }
-  if (final_state) {
-#pragma unroll
-    for (int nt = 0; nt < 16; ++nt)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int dv = dv0 + gq + (j >> 1) * 8, dk = nt * 8 + 2 * tq + (j & 1);
-        final_state[(((int64_t)s * heads + h) * DR_D + dk) * DR_D + dv] = st[nt][j];
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&mw);
+      prefetch_tmap(&mqg);
+      prefetch_tmap(&mkg);
+      prefetch_tmap(&ma);
+      int issued = 0;
+      for (int c = 0; c < nch; ++c) {
+        const int st = c & 1;
+        if (c >= 2 && !mbar_wait(bar0 + 8 * (B_EMPTY0 + st), ((c >> 1) - 1) & 1, abort_flag)) break;
+        const uint32_t sb = base + st * ST_BYTES;
+        const uint32_t fb = bar0 + 8 * (B_FULL0 + st);
+        const int z = (c0 + c) * H + h;
+        mbar_expect_tx(fb, ST_BYTES);
+        tma_load_3d(sb + ST_W, &mw, fb, 0, 0, z);
+        tma_load_3d(sb + ST_W + KM_HALF, &mw, fb, 64, 0, z);
+        tma_load_3d(sb + ST_QG, &mqg, fb, 0, 0, z);
+        tma_load_3d(sb + ST_QG + KM_HALF, &mqg, fb, 64, 0, z);
+        tma_load_3d(sb + ST_KG, &mkg, fb, 0, 0, z);
+        tma_load_3d(sb + ST_KG + KM_HALF, &mkg, fb, 64, 0, z);
+        tma_load_3d(sb + ST_A, &ma, fb, 0, 0, z);
+        issued = c + 1;
       }
+      // before the CTA exits, every issued copy has landed (the last two stages' phases are the
+      // newest ones of their barriers, so these parity waits cannot alias)
+      volatile int never = 0;
+      for (int c = issued > 2 ? issued - 2 : 0; c < issued; ++c)
+        mbar_wait(bar0 + 8 * (B_FULL0 + (c & 1)), (c >> 1) & 1, &never, DRAIN_BUDGET);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t ID_N64 = idesc_bf16(128, 64, false, false);
+      constexpr uint32_t ID_N128_BMN = idesc_bf16(128, 128, false, true);
+      for (int c = 0; c < nch; ++c) {
+        const int st = c & 1;
+        const uint32_t sb = base + st * ST_BYTES;
+        if (!mbar_wait(bar0 + 8 * (B_FULL0 + st), (c >> 1) & 1, abort_flag)) break;
+        if (!mbar_wait(bar0 + 8 * B_SA, c & 1, abort_flag)) break;
+        tc_fence_after();
+        // vn = S^T W^T and o^T = S^T Qg^T   (K = 128 dk: 2 swizzle halves x 4 steps of 16)
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t aoff = (uint32_t)(kk >> 2) * (128u * 128u) + (uint32_t)(kk & 3) * 32u;
+          const uint32_t boff = (uint32_t)(kk >> 2) * KM_HALF + (uint32_t)(kk & 3) * 32u;
+          const uint64_t ad = sdesc_sw128(base + OFF_SA + aoff, 16, 1024);
+          umma_ss(tmem + TM_VN, ad, sdesc_sw128(sb + ST_W + boff, 16, 1024), ID_N64, kk > 0 ? 1u : 0u);
+          umma_ss(tmem + TM_O, ad, sdesc_sw128(sb + ST_QG + boff, 16, 1024), ID_N64, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(bar0 + 8 * B_VN);
+        if (!mbar_wait(bar0 + 8 * B_VNEW, c & 1, abort_flag)) break;
+        tc_fence_after();
+        // S^T += v_new^T Kg  (Kg MN-major: [2 dk halves][64 tok][128 B]; K = 64 tokens in 4 steps)
+        // o^T += v_new^T Aqk^T
+#pragma unroll
+        for (int kt = 0; kt < 4; ++kt) {
+          const uint64_t ad = sdesc_sw128(base + OFF_VA + kt * 32, 16, 1024);
+          umma_ss(tmem + TM_S, ad, sdesc_sw128(sb + ST_KG + kt * 2048, KM_HALF, 1024), ID_N128_BMN, 1u);
+          umma_ss(tmem + TM_O, ad, sdesc_sw128(sb + ST_A + kt * 32, 16, 1024), ID_N64, 1u);
+        }
+        umma_commit(bar0 + 8 * B_SDONE);
+        umma_commit(bar0 + 8 * (B_EMPTY0 + st));
+      }
+      // every MMA issued above has completed before TMEM is freed
+      volatile int never = 0;
+      umma_commit(bar0 + 8 * B_DRAIN);
+      mbar_wait(bar0 + 8 * B_DRAIN, 0, &never, DRAIN_BUDGET);
+    }
+  } else {
+    // ---------------------------------------------------------------- state warps (128 threads)
+    const int q4 = warp & 3;       // the TMEM lane quarter this warp may access
+    const int r = q4 * 32 + lane;  // dv row == TMEM lane
+    const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
+    const uint32_t tS = tmem + lane_addr + TM_S, tVN = tmem + lane_addr + TM_VN, tO = tmem + lane_addr + TM_O;
+    const int64_t sh = (int64_t)s * H + h;
+    uint8_t* sa = gbase + OFF_SA;
+    uint8_t* va = gbase + OFF_VA;
+    bf16* ost = reinterpret_cast<bf16*>(gbase + OFF_OST) + q4 * (64 * 32);  // [64 tok][32 dv] of this warp
+
+    // S^T[r][dk] = initial_state[dk][r]
+#pragma unroll
+    for (int cb = 0; cb < 4; ++cb) {
+      uint32_t v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        v[i] = __float_as_uint(p.init_state ? p.init_state[(sh * DR_D + cb * 32 + i) * DR_D + r] : 0.f);
+      tmem_st32(tS + cb * 32, v);
+    }
+    tmem_st_wait();
+
+    // o^T of chunk c (complete in TMEM) -> out[token][h][dv], 64-byte pieces per token
+    auto o_epilogue = [&](int c) {
+      uint32_t o[2][32];
+      tmem_ld32(tO, o[0]);
+      tmem_ld32(tO + 32, o[1]);
+      tmem_ld_wait();
+#pragma unroll
+      for (int t = 0; t < 64; ++t) ost[t * 32 + lane] = __float2bfloat16_rn(__uint_as_float(o[t >> 5][t & 31]));
+      __syncwarp();
+      const int tok0 = seg_t0 + c * DR_C;
+      const int len = min(DR_C, seg_len - c * DR_C);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int e = lane + i * 32, tr = e >> 2, ch = e & 3;
+        if (tr < len)
+          *reinterpret_cast<uint4*>(p.out + ((int64_t)(tok0 + tr) * H + h) * DR_D + q4 * 32 + ch * 8) =
+              *reinterpret_cast<const uint4*>(ost + tr * 32 + ch * 8);
+      }
+      __syncwarp();
+    };
+    auto load_u = [&](int c, uint4 (&u)[8], float& g) {
+      const uint8_t* tile = p.tiles + ((size_t)(c0 + c) * H + h) * CH_BYTES;
+      const uint4* row = reinterpret_cast<const uint4*>(tile + OFF_UT + (size_t)r * DR_C * 2);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) u[i] = __ldg(row + i);
+      g = __ldg(reinterpret_cast<const float*>(tile + OFF_GAMMA));
+    };
+
+    bool ok = true;
+    uint4 ut[8];  // U^T row r of the current chunk, and gamma; prefetched one chunk ahead
+    float gam = 1.f;
+    if (nch > 0) load_u(0, ut, gam);
+    for (int c = 0; c < nch; ++c) {
+      if (c > 0) {
+        if (!warp_wait(bar0 + 8 * B_SDONE, (c - 1) & 1, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        o_epilogue(c - 1);
+      }
+      uint4 ut_next[8];
+      float gam_next = 1.f;
+      if (c + 1 < nch) load_u(c + 1, ut_next, gam_next);
+      // S^T -> bf16 A tile; S^T *= gamma_c in TMEM (the MMAs of this chunk read the A tile)
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb) {
+        uint32_t v[32];
+        tmem_ld32(tS + cb * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float f[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(v[j * 8 + i]);
+          *reinterpret_cast<uint4*>(sa + sw128_off(r, cb * 4 + j, 128)) = pack8(f);
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * gam);
+        tmem_st32(tS + cb * 32, v);
+      }
+      tmem_st_wait();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(bar0 + 8 * B_SA);
+      // v_new^T = U^T - vn -> bf16 A tile
+      if (!warp_wait(bar0 + 8 * B_VN, c & 1, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      {
+        uint32_t v[2][32];
+        tmem_ld32(tVN, v[0]);
+        tmem_ld32(tVN + 32, v[1]);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float u[8], f[8];
+          unpack8(ut[j], u);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) f[i] = u[i] - __uint_as_float(v[j >> 2][(j & 3) * 8 + i]);
+          *reinterpret_cast<uint4*>(va + sw128_off(r, j, 128)) = pack8(f);
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(bar0 + 8 * B_VNEW);
+      if (c + 1 < nch) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ut[i] = ut_next[i];
+        gam = gam_next;
+      }
+    }
+    if (ok && nch > 0) {
+      ok = warp_wait(bar0 + 8 * B_SDONE, (nch - 1) & 1, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        o_epilogue(nch - 1);
+      }
+    }
+    if (ok && p.final_state) {
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb) {
+        uint32_t v[32];
+        tmem_ld32(tS + cb * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) p.final_state[(sh * DR_D + cb * 32 + i) * DR_D + r] = __uint_as_float(v[i]);
+      }
+    }
   }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TM_COLS);
+  }
+  if (tid == 0 && *abort_flag) atomicExch(&g_recur_error, 1);
 }
 
-template <int WARPS>
-static int launch_recur(int nseg, int heads, cudaStream_t s, const int32_t* cu, const int32_t* table,
+using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
+
+static EncodeFn encode_fn() {
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(ptr);
+    cudaGetLastError();
+  }
+  return fn;
+}
+
+// 3-D map over one operand of every workspace tile: [n_tiles][64 rows][cols] bf16, tile stride
+// CH_BYTES, box 64 x 64 x 1, 128-byte swizzle.
+static int tile_map(CUtensorMap* m, const uint8_t* tiles, size_t off, int cols, int64_t n_tiles) {
+  EncodeFn enc = encode_fn();
+  if (!enc) return set_error(FDK_ERR_DEVICE, "chunk_gated_delta_rule: cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)DR_C, (cuuint64_t)n_tiles};
+  cuuint64_t strides[2] = {(cuuint64_t)cols * 2, (cuuint64_t)CH_BYTES};
+  cuuint32_t box[3] = {64, 64, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<uint8_t*>(tiles + off), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(FDK_ERR_INVALID_ARGUMENT, "chunk_gated_delta_rule: tensor map encode failed (%d)", (int)r);
+  return FDK_OK;
+}
+
+}  // namespace drtc
+
+int delta_take_device_error() {
+  int h = 0;
+  if (cudaMemcpyFromSymbol(&h, drtc::g_recur_error, sizeof(int)) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  if (h) {
+    int zero = 0;
+    cudaMemcpyToSymbol(drtc::g_recur_error, &zero, sizeof(int));
+  }
+  return h;
+}
+
+static int launch_recur(int nseg, int heads, int64_t n_tiles, cudaStream_t s, const int32_t* cu, const int32_t* table,
                         const uint8_t* tiles, const float* init, bf16* out, float* fin) {
-  const int smem = (int)sizeof(RecurSmem<WARPS>);
+  using namespace drtc;
+  CUtensorMap mw, mqg, mkg, ma;
+  if (int st = tile_map(&mw, tiles, OFF_W, DR_D, n_tiles)) return st;
+  if (int st = tile_map(&mqg, tiles, OFF_QG, DR_D, n_tiles)) return st;
+  if (int st = tile_map(&mkg, tiles, OFF_KG, DR_D, n_tiles)) return st;
+  if (int st = tile_map(&ma, tiles, OFF_A, DR_C, n_tiles)) return st;
+  const RParams prm{cu, table, heads, tiles, init, out, fin};
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaFuncSetAttribute(delta_recur_kernel<WARPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(delta_recur_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  delta_recur_kernel<WARPS><<<dim3((unsigned)nseg, (unsigned)heads, DR_D / (16 * WARPS)), WARPS * 32, smem, s>>>(
-      cu, nseg, table, heads, tiles, init, out, fin);
+  delta_recur_tc_kernel<<<dim3((unsigned)nseg, (unsigned)heads), THREADS, SMEM_BYTES, s>>>(mw, mqg, mkg, ma, prm);
   return check_launch("chunk_gated_delta_rule/recurrence");
 }
 
@@ -620,7 +756,7 @@ extern "C" int fdk_chunk_gated_delta_rule_fwd(const void* q, const void* k, int6
   const int nseg = (int)num_segments;
   chunk_table_kernel<<<1, 32, 0, s>>>(cu_seqlens, nseg, table);
   if (int st = check_launch("chunk_gated_delta_rule/table")) return st;
-  if (tokens == 0) return FDK_OK;
+  if (tokens == 0 && !final_state) return FDK_OK;
   static bool attr_set[64] = {};
   const int prep_smem = (int)sizeof(PrepSmem);
   int dev = 0;
@@ -629,19 +765,14 @@ extern "C" int fdk_chunk_gated_delta_rule_fwd(const void* q, const void* k, int6
     cudaFuncSetAttribute(delta_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem);
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  delta_prep_kernel<<<dim3((unsigned)lay.max_chunks, (unsigned)heads), PREP_THREADS, prep_smem, s>>>(
-      static_cast<const bf16*>(q), static_cast<const bf16*>(k), ld_qk, static_cast<const bf16*>(v), ld_v, g,
-      static_cast<const bf16*>(beta), cu_seqlens, nseg, table, (int)heads, scale, tiles);
-  if (int st = check_launch("chunk_gated_delta_rule/prep")) return st;
-  // Few (segment, head) pairs: one warp per 16 dv rows spreads the sequential chains over more
-  // SMs; many pairs: 4 warps share each chunk tile read.
-  const int64_t pairs = (int64_t)nseg * heads;
-  auto o = static_cast<bf16*>(out);
-  if (pairs * 8 <= 2 * (int64_t)sm_count())
-    return launch_recur<1>(nseg, (int)heads, s, cu_seqlens, table, tiles, initial_state, o, final_state);
-  if (pairs * 4 <= 2 * (int64_t)sm_count())
-    return launch_recur<2>(nseg, (int)heads, s, cu_seqlens, table, tiles, initial_state, o, final_state);
-  return launch_recur<4>(nseg, (int)heads, s, cu_seqlens, table, tiles, initial_state, o, final_state);
+  if (tokens > 0) {
+    delta_prep_kernel<<<dim3((unsigned)lay.max_chunks, (unsigned)heads), PREP_THREADS, prep_smem, s>>>(
+        static_cast<const bf16*>(q), static_cast<const bf16*>(k), ld_qk, static_cast<const bf16*>(v), ld_v, g,
+        static_cast<const bf16*>(beta), cu_seqlens, nseg, table, (int)heads, scale, tiles);
+    if (int st = check_launch("chunk_gated_delta_rule/prep")) return st;
+  }
+  return launch_recur(nseg, (int)heads, lay.max_chunks * heads, s, cu_seqlens, table, tiles, initial_state,
+                      static_cast<bf16*>(out), final_state);
 }
 
 // ---------------------------------------------------------------------------------------------

@@ -284,6 +284,16 @@ def test_delta_rule_initial_state():
     delta_check(150, 2, 6, cu=[0, 70, 150], init=True)
 
 
+def test_delta_rule_empty_segments_keep_initial_state():
+    # empty segments at both ends: their final state is the initial state, untouched
+    delta_check(150, 2, 8, cu=[0, 0, 150, 150], init=True)
+
+
+def test_delta_rule_long_segment_many_heads():
+    # 40 chunks per (segment, head) through the 2-stage tile ring, plus a ragged short segment
+    delta_check(2600, 8, 9, cu=[0, 2560, 2600], init=True)
+
+
 def test_delta_rule_golden(golden):
     f = golden["delta_d128"]
     o, st = ops.chunk_gated_delta_rule(dev(f["q"].bfloat16()), dev(f["k"].bfloat16()), dev(f["v"].bfloat16()),
