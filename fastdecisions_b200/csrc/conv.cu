@@ -30,22 +30,18 @@ __device__ __forceinline__ int64_t next_start(const int32_t* cu, int nseg, int64
   return cu[lo];
 }
 
-__device__ __forceinline__ void unpack4(const uint2& u, float (&f)[4]) {
-  float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-  float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
-  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
-}
-
-// Shared-memory staged variant (the one launched): a CTA owns a 128-channel column block and
-// CONV_TILES_PER_CTA consecutive 64-token tiles.  Tile rows [t0 - 3, t0 + 64) (the 3-row causal
-// halo included) stream into shared memory with cp.async, double-buffered, so the next tile's
-// 16-byte loads are in flight while the current one is convolved.  Thread (cq, rg) computes 4
-// channels x 16 rows with the taps in registers; a warp stores 256 contiguous bytes per row.
+// Shared-memory staged kernel: a CTA owns a 128-channel column block and CONV_TILES_PER_CTA
+// consecutive 64-token tiles.  Tile rows [t0 - 3, t0 + 64) (the 3-row causal halo included) stream
+// into shared memory with cp.async, double-buffered, so the next tile's 16-byte loads are in flight
+// while the current one is convolved.  Thread (cq, rg) computes 8 channels x 8 rows with the taps
+// in registers (16-byte shared loads and global stores); a half-warp stores 256 contiguous bytes
+// per row.  SiLU uses the one-MUFU tanh form: the MUFU pipe, not HBM, bounded the two-op form.
 constexpr int CONV_CB = 128;            // channels per CTA
 constexpr int CONV_ROWS = 64;           // tokens per tile
 constexpr int CONV_HALO = 3;
 constexpr int CONV_TILES_PER_CTA = 4;
 constexpr int CONV_SROWS = CONV_ROWS + CONV_HALO;
+constexpr int CONV_RPT = 8;             // rows per thread
 
 template <int KW>
 __global__ void __launch_bounds__(CONV_THREADS) packed_conv_silu_smem_kernel(
@@ -55,8 +51,8 @@ __global__ void __launch_bounds__(CONV_THREADS) packed_conv_silu_smem_kernel(
   __shared__ __align__(16) bf16 tile[2][CONV_SROWS][CONV_CB];
   const int tid = threadIdx.x;
   const int cb0 = blockIdx.x * CONV_CB;
-  const int cq = tid & 31, rg = tid >> 5;   // 4 channels, 16 rows
-  const int c0 = cb0 + cq * 4;
+  const int cq = tid & 15, rg = tid >> 4;   // 8 channels, 8 rows
+  const int c0 = cb0 + cq * 8;
   const int64_t first = (int64_t)blockIdx.y * CONV_TILES_PER_CTA;
   const int64_t ntiles = (ntok + CONV_ROWS - 1) / CONV_ROWS;
   const int64_t last = (first + CONV_TILES_PER_CTA < ntiles) ? first + CONV_TILES_PER_CTA : ntiles;
@@ -65,7 +61,7 @@ __global__ void __launch_bounds__(CONV_THREADS) packed_conv_silu_smem_kernel(
   auto issue = [&](int64_t ti, int b) {
     const int64_t base = ti * CONV_ROWS - CONV_HALO;
     for (int e = tid; e < CONV_SROWS * (CONV_CB / 8); e += CONV_THREADS) {
-      const int r = e / (CONV_CB / 8), ch = (e % (CONV_CB / 8)) * 8;
+      const int r = e >> 4, ch = (e & 15) * 8;
       const int64_t t = base + r;
       const bool ok = t >= 0 && t < ntok && cb0 + ch < channels;
       const bf16* src = x + (ok ? t : 0) * ldx + (ok ? cb0 + ch : 0);
@@ -76,9 +72,9 @@ __global__ void __launch_bounds__(CONV_THREADS) packed_conv_silu_smem_kernel(
   };
 
   const bool active = c0 < channels;  // the last column block may be partial (threads still sync)
-  float wr[KW][4];
+  float wr[KW][8];
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
+  for (int c = 0; c < 8; ++c) {
     const bf16* wc = w + (int64_t)(active ? c0 + c : 0) * KW;
 #pragma unroll
     for (int j = 0; j < KW; ++j) wr[j][c] = __bfloat162float(wc[j]);
@@ -100,8 +96,8 @@ __global__ void __launch_bounds__(CONV_THREADS) packed_conv_silu_smem_kernel(
       asm volatile("cp.async.wait_group 0;\n" ::);
     }
     __syncthreads();
-    const int64_t r0 = ti * CONV_ROWS + rg * 16;   // first output token of this thread
-    if (active) {  // predicated, never around a barrier: every thread reaches both __syncthreads
+    const int64_t r0 = ti * CONV_ROWS + rg * CONV_RPT;   // first output token of this thread
+    if (active && r0 < ntok) {  // predicated, never around a barrier: every thread reaches both __syncthreads
       int64_t seg0, nxt;
       if (cu != nullptr) {
         seg0 = segment_start(cu, nseg, r0);
@@ -110,44 +106,41 @@ __global__ void __launch_bounds__(CONV_THREADS) packed_conv_silu_smem_kernel(
         seg0 = (r0 / period) * period;
         nxt = seg0 + period;
       }
-      float hist[3][4];
+      float hist[3][8];
 #pragma unroll
       for (int j = 0; j < 3; ++j) {
         const int64_t t = r0 - 3 + j;
-        const int sr = rg * 16 + j;  // smem row of token t
-        if (t >= seg0) unpack4(*reinterpret_cast<const uint2*>(&tile[b][sr][cq * 4]), hist[j]);
+        if (t >= seg0) unpack8(*reinterpret_cast<const uint4*>(&tile[b][rg * CONV_RPT + j][cq * 8]), hist[j]);
         else {
 #pragma unroll
-          for (int c = 0; c < 4; ++c) hist[j][c] = 0.f;
+          for (int c = 0; c < 8; ++c) hist[j][c] = 0.f;
         }
       }
+      bf16* out = dst + r0 * ldd + cc;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < CONV_RPT; ++i) {
         const int64_t t = r0 + i;
         if (t < ntok) {
           if (t == nxt) {
 #pragma unroll
             for (int j = 0; j < 3; ++j)
 #pragma unroll
-              for (int c = 0; c < 4; ++c) hist[j][c] = 0.f;
+              for (int c = 0; c < 8; ++c) hist[j][c] = 0.f;
             nxt = (cu != nullptr) ? next_start(cu, nseg, t) : nxt + period;
           }
-          float cur[4], y[4];
-          unpack4(*reinterpret_cast<const uint2*>(&tile[b][rg * 16 + CONV_HALO + i][cq * 4]), cur);
+          float cur[8], y[8];
+          unpack8(*reinterpret_cast<const uint4*>(&tile[b][rg * CONV_RPT + CONV_HALO + i][cq * 8]), cur);
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < 8; ++c) {
             float acc = wr[KW - 1][c] * cur[c];
             if (KW >= 2) acc = fmaf(wr[KW - 2][c], hist[2][c], acc);
             if (KW >= 3) acc = fmaf(wr[KW - 3][c], hist[1][c], acc);
             if (KW >= 4) acc = fmaf(wr[KW - 4][c], hist[0][c], acc);
-            y[c] = silu(acc);
+            y[c] = silu_tanh(acc);
           }
-          uint2 o;
-          o.x = pack_bf16x2(y[0], y[1]);
-          o.y = pack_bf16x2(y[2], y[3]);
-          *reinterpret_cast<uint2*>(dst + t * ldd + cc) = o;
+          *reinterpret_cast<uint4*>(out + i * ldd) = pack8(y);
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < 8; ++c) {
             hist[0][c] = hist[1][c];
             hist[1][c] = hist[2][c];
             hist[2][c] = cur[c];

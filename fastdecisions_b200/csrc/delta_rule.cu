@@ -47,7 +47,7 @@ __host__ __device__ inline WsLayout ws_layout(int64_t tokens, int64_t nseg, int6
   WsLayout l;
   l.max_chunks = (tokens + DR_C - 1) / DR_C + nseg;
   l.off_table = 0;
-  l.off_tiles = align256((size_t)(nseg + 1) * 4);
+  l.off_tiles = align256((size_t)(nseg + 2) * 4);  // chunk table [nseg + 1] + work counter
   l.total = l.off_tiles + align256((size_t)l.max_chunks * heads * CH_BYTES);
   return l;
 }
@@ -99,7 +99,10 @@ __global__ void chunk_table_kernel(const int32_t* __restrict__ cu, int nseg, int
     if (s < nseg) table[s] = carry + incl - n;
     carry += __shfl_sync(0xffffffffu, incl, 31);
   }
-  if (lane == 0) table[nseg] = carry;
+  if (lane == 0) {
+    table[nseg] = carry;
+    table[nseg + 1] = 0;  // work counter of the recurrence
+  }
 }
 
 // ------------------------------------------------------------------------------------------ prep
@@ -337,7 +340,7 @@ __global__ void __launch_bounds__(PREP_THREADS, 2) delta_prep_kernel(
       }
     }
     __syncthreads();  // every warp is done with TU/TW, k and v: stage W and U^T there
-    __nv_bfloat16* Wst = sm.q;   // [64][128] plain row-major
+    __nv_bfloat16* Wst = sm.q;   // [64][128] swizzled (conflict-free fragment stores)
     __nv_bfloat16* Ust = sm.k;   // [128][UT_LD] transposed, padded (spans k and v)
 #pragma unroll
     for (int n = 0; n < 8; ++n)
@@ -345,18 +348,17 @@ __global__ void __launch_bounds__(PREP_THREADS, 2) delta_prep_kernel(
       for (int hh = 0; hh < 2; ++hh) {
         const int i = r0 + gq + hh * 8;
         const int j = n0 + n * 8 + 2 * tq;
-        *reinterpret_cast<uint32_t*>(&Wst[i * DR_D + j]) = pack_bf16x2(w[n][hh * 2], w[n][hh * 2 + 1]);
+        *reinterpret_cast<uint32_t*>(&Wst[swz<DR_D>(i, j)]) = pack_bf16x2(w[n][hh * 2], w[n][hh * 2 + 1]);
         Ust[j * UT_LD + i] = __float2bfloat16_rn(u[n][hh * 2]);
         Ust[(j + 1) * UT_LD + i] = __float2bfloat16_rn(u[n][hh * 2 + 1]);
       }
   }
   __syncthreads();
   {
-    const uint4* sW = reinterpret_cast<const uint4*>(sm.q);
     uint4* gW = reinterpret_cast<uint4*>(tile + OFF_W);
     __nv_bfloat16* gU = reinterpret_cast<__nv_bfloat16*>(tile + OFF_UT);
     for (int e = tid; e < (int)(TILE128 / 16); e += PREP_THREADS) {
-      gW[e] = sW[e];
+      gW[e] = *reinterpret_cast<const uint4*>(&sm.q[swz<DR_D>(e >> 4, (e & 15) << 3)]);
       const int j = e >> 3, c = (e & 7) << 3;
       *reinterpret_cast<uint4*>(gU + j * DR_C + c) = *reinterpret_cast<const uint4*>(sm.k + j * UT_LD + c);
     }
@@ -365,31 +367,34 @@ __global__ void __launch_bounds__(PREP_THREADS, 2) delta_prep_kernel(
 }
 
 // ------------------------------------------------------------------------------------- recurrence
-// tcgen05 recurrence: one CTA per (segment, head), sequential over the segment's chunks.
-//   TMEM (256 columns of fp32; lane = dv row): S^T [0,128), vn [128,192), o^T [192,256).
-//   Per chunk c, with W, Qg, Kg, Aqk of chunk c in a 2-stage TMA ring (128-byte swizzle):
-//     state warps : o^T of chunk c-1 -> out; S^T -> bf16 A tile in SMEM; S^T *= gamma_c in TMEM
-//     MMA thread  : vn  = S^T W^T            (M128 N64  K128)
-//                   o^T = S^T Qg^T           (M128 N64  K128)
-//     state warps : v_new^T = U^T - vn -> bf16 A tile in SMEM
-//     MMA thread  : S^T += v_new^T Kg        (M128 N128 K64; Kg is MN-major)
-//                   o^T += v_new^T Aqk^T     (M128 N64  K64)
-//   Warps: 0 TMA producer, 1 TMEM allocator + single-thread MMA issuer, 2-5 state warps (one
-//   thread per dv row = TMEM lane).  Every mbarrier wait is bounded; a wait that runs out sets the
-//   device error word and the CTA drains its copies and MMAs, frees TMEM and returns.
+// tcgen05 recurrence, persistent: each CTA takes (segment, head) chains from an atomic work counter
+// and runs them chunk by chunk; the tile ring runs ahead across chain boundaries.
+//   TMEM (512 columns of fp32; lane = dv row): S^T [0,128), vn [128,192), o^T [192,256) and
+//   [256,320) (double-buffered so the output epilogue leaves the critical path).
+//   Per chunk n (tiles W, Qg, Kg, Aqk, U^T of the chunk in a 2-stage TMA ring, 128-byte swizzle):
+//     state warps : S^T -> bf16 A tile in SMEM; S^T *= gamma in TMEM
+//     MMA thread  : vn = S^T W^T (M128 N64 K128); then o^T = S^T Qg^T
+//     state warps : v_new^T = U^T - vn -> bf16 A tile in SMEM; then o^T of chunk n-1 -> out
+//     MMA thread  : S^T += v_new^T Kg (M128 N128 K64, Kg MN-major); then o^T += v_new^T Aqk^T
+//   Warps: 0 TMA producer (and work counter), 1 TMEM allocator + single-thread MMA issuer, 2-5
+//   state warps (one thread per dv row = TMEM lane).  Every mbarrier wait is bounded; a wait that
+//   runs out sets the device error word, and the CTA drains its copies and MMAs, frees TMEM and
+//   returns.
 namespace drtc {
 using namespace sm100;
 
 constexpr uint32_t KM_HALF = 64 * 128;  // [64 rows][128 B] swizzled block (one TMA box)
-constexpr uint32_t ST_W = 0, ST_QG = 2 * KM_HALF, ST_KG = 4 * KM_HALF, ST_A = 6 * KM_HALF, ST_BYTES = 7 * KM_HALF;
+constexpr uint32_t ST_W = 0, ST_QG = 2 * KM_HALF, ST_KG = 4 * KM_HALF, ST_A = 6 * KM_HALF, ST_UT = 7 * KM_HALF,
+                   ST_BYTES = 9 * KM_HALF;           // U^T: [128 dv][128 B]
 constexpr uint32_t OFF_SA = 2 * ST_BYTES;            // S^T bf16 A tile: [2 dk halves][128 dv][128 B]
 constexpr uint32_t OFF_VA = OFF_SA + 2 * 128 * 128;  // v_new^T bf16 A tile: [128 dv][128 B]
 constexpr uint32_t OFF_OST = OFF_VA + 128 * 128;     // o staging: per state warp [64 tok][32 dv] bf16
-constexpr uint32_t OFF_BAR = OFF_OST + 4 * 64 * 32 * 2;
-enum { B_FULL0 = 0, B_FULL1, B_EMPTY0, B_EMPTY1, B_SA, B_VN, B_VNEW, B_SDONE, B_DRAIN, NBAR };
+constexpr uint32_t OFF_META = OFF_OST + 4 * 64 * 32 * 2;
+constexpr uint32_t OFF_BAR = OFF_META + 2 * 32;
+enum { B_FULL0 = 0, B_FULL1, B_EMPTY0, B_EMPTY1, B_SA, B_VN, B_VNEW, B_SDONE, B_ODONE0, B_ODONE1, B_DRAIN, NBAR };
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 8 * NBAR + 16 + 1024;
 constexpr int THREADS = 192;
-constexpr uint32_t TM_S = 0, TM_VN = 128, TM_O = 192, TM_COLS = 256;
+constexpr uint32_t TM_S = 0, TM_VN = 128, TM_O = 192, TM_COLS = 512;
 constexpr long long DRAIN_BUDGET = 2000000000LL;
 
 __device__ int g_recur_error = 0;
@@ -397,11 +402,18 @@ __device__ int g_recur_error = 0;
 struct RParams {
   const int32_t* cu;
   const int32_t* table;
-  int heads;
-  const uint8_t* tiles;  // workspace tiles (U^T rows and gamma are read from here directly)
+  int32_t* work_counter;  // zeroed by the chunk-table kernel of the same call
+  int nseg, heads;
+  const uint8_t* tiles;   // gamma is read from here directly
   const float* init_state;
   bf16* out;
   float* final_state;
+};
+
+struct StageMeta {  // written by the producer before the stage's expect_tx arrive
+  int s, h, c, nch;
+  float gamma;
+  int pad[3];
 };
 
 // byte offset of 16-byte chunk `c16` of row `r` in a [c16 / 8][rows][128 B] 128-byte-swizzled tile
@@ -418,7 +430,7 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
 __global__ void __launch_bounds__(THREADS, 1)
 delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_constant__ CUtensorMap mqg,
                       const __grid_constant__ CUtensorMap mkg, const __grid_constant__ CUtensorMap ma,
-                      const RParams p) {
+                      const __grid_constant__ CUtensorMap mut, const RParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -426,10 +438,9 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
   const uint32_t bar0 = base + OFF_BAR;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + OFF_BAR + 8 * NBAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_BAR + 8 * NBAR + 4);
+  volatile StageMeta* meta = reinterpret_cast<volatile StageMeta*>(gbase + OFF_META);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int s = blockIdx.x, h = blockIdx.y, H = p.heads;
-  const int c0 = p.table[s], nch = p.table[s + 1] - c0;
-  const int seg_t0 = p.cu[s], seg_len = p.cu[s + 1] - p.cu[s];
+  const int H = p.heads;
 
   if (tid == 0) {
     for (int i = 0; i < NBAR; ++i) mbar_init(bar0 + 8 * i, (i == B_SA || i == B_VNEW) ? 128u : 1u);
@@ -452,61 +463,98 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
       prefetch_tmap(&mqg);
       prefetch_tmap(&mkg);
       prefetch_tmap(&ma);
-      int issued = 0;
-      for (int c = 0; c < nch; ++c) {
-        const int st = c & 1;
-        if (c >= 2 && !mbar_wait(bar0 + 8 * (B_EMPTY0 + st), ((c >> 1) - 1) & 1, abort_flag)) break;
-        const uint32_t sb = base + st * ST_BYTES;
-        const uint32_t fb = bar0 + 8 * (B_FULL0 + st);
-        const int z = (c0 + c) * H + h;
-        mbar_expect_tx(fb, ST_BYTES);
-        tma_load_3d(sb + ST_W, &mw, fb, 0, 0, z);
-        tma_load_3d(sb + ST_W + KM_HALF, &mw, fb, 64, 0, z);
-        tma_load_3d(sb + ST_QG, &mqg, fb, 0, 0, z);
-        tma_load_3d(sb + ST_QG + KM_HALF, &mqg, fb, 64, 0, z);
-        tma_load_3d(sb + ST_KG, &mkg, fb, 0, 0, z);
-        tma_load_3d(sb + ST_KG + KM_HALF, &mkg, fb, 64, 0, z);
-        tma_load_3d(sb + ST_A, &ma, fb, 0, 0, z);
-        issued = c + 1;
+      prefetch_tmap(&mut);
+      const int items = p.nseg * H;
+      int n = 0;  // real chunks pushed into the ring by this CTA
+      bool closed = false;
+      while (true) {
+        const int item = atomicAdd(p.work_counter, 1);
+        if (item >= items) {  // closing stage: s = -1, no tiles
+          const int st = n & 1;
+          if (n >= 2 && !mbar_wait(bar0 + 8 * (B_EMPTY0 + st), ((n >> 1) - 1) & 1, abort_flag)) break;
+          meta[st].s = -1;
+          mbar_arrive(bar0 + 8 * (B_FULL0 + st));
+          closed = true;
+          break;
+        }
+        const int s = item / H, h = item - s * H;
+        const int c0 = __ldg(p.table + s), nch = __ldg(p.table + s + 1) - c0;
+        bool ok = true;
+        for (int c = 0; c < nch; ++c, ++n) {
+          const int st = n & 1;
+          if (n >= 2 && !mbar_wait(bar0 + 8 * (B_EMPTY0 + st), ((n >> 1) - 1) & 1, abort_flag)) { ok = false; break; }
+          const int z = (c0 + c) * H + h;
+          meta[st].s = s;
+          meta[st].h = h;
+          meta[st].c = c;
+          meta[st].nch = nch;
+          meta[st].gamma = __ldg(reinterpret_cast<const float*>(p.tiles + (size_t)z * CH_BYTES + OFF_GAMMA));
+          const uint32_t sb = base + st * ST_BYTES;
+          const uint32_t fb = bar0 + 8 * (B_FULL0 + st);
+          mbar_expect_tx(fb, ST_BYTES);
+          tma_load_3d(sb + ST_W, &mw, fb, 0, 0, z);
+          tma_load_3d(sb + ST_W + KM_HALF, &mw, fb, 64, 0, z);
+          tma_load_3d(sb + ST_QG, &mqg, fb, 0, 0, z);
+          tma_load_3d(sb + ST_QG + KM_HALF, &mqg, fb, 64, 0, z);
+          tma_load_3d(sb + ST_KG, &mkg, fb, 0, 0, z);
+          tma_load_3d(sb + ST_KG + KM_HALF, &mkg, fb, 64, 0, z);
+          tma_load_3d(sb + ST_A, &ma, fb, 0, 0, z);
+          tma_load_3d(sb + ST_UT, &mut, fb, 0, 0, z);
+        }
+        if (!ok) break;
       }
-      // before the CTA exits, every issued copy has landed (the last two stages' phases are the
-      // newest ones of their barriers, so these parity waits cannot alias)
+      // Before the CTA exits every issued copy has landed.  Real chunk m's phase is the newest of
+      // its FULL barrier unless the closing stage followed on the same barrier, which it only did
+      // after chunk m's tiles were consumed.
       volatile int never = 0;
-      for (int c = issued > 2 ? issued - 2 : 0; c < issued; ++c)
-        mbar_wait(bar0 + 8 * (B_FULL0 + (c & 1)), (c >> 1) & 1, &never, DRAIN_BUDGET);
+      for (int m = n > 2 ? n - 2 : 0; m < n; ++m)
+        if (!(closed && ((m ^ n) & 1) == 0))
+          mbar_wait(bar0 + 8 * (B_FULL0 + (m & 1)), (m >> 1) & 1, &never, DRAIN_BUDGET);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t ID_N64 = idesc_bf16(128, 64, false, false);
       constexpr uint32_t ID_N128_BMN = idesc_bf16(128, 128, false, true);
-      for (int c = 0; c < nch; ++c) {
-        const int st = c & 1;
+      for (int n = 0;; ++n) {
+        const int st = n & 1;
         const uint32_t sb = base + st * ST_BYTES;
-        if (!mbar_wait(bar0 + 8 * (B_FULL0 + st), (c >> 1) & 1, abort_flag)) break;
-        if (!mbar_wait(bar0 + 8 * B_SA, c & 1, abort_flag)) break;
+        if (!mbar_wait(bar0 + 8 * (B_FULL0 + st), (n >> 1) & 1, abort_flag)) break;
+        if (meta[st].s < 0) break;
+        if (!mbar_wait(bar0 + 8 * B_SA, n & 1, abort_flag)) break;
         tc_fence_after();
-        // vn = S^T W^T and o^T = S^T Qg^T   (K = 128 dk: 2 swizzle halves x 4 steps of 16)
+        const uint32_t tO = tmem + TM_O + 64u * (uint32_t)st;
+        // vn = S^T W^T  (K = 128 dk: 2 swizzle halves x 4 steps of 16)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t aoff = (uint32_t)(kk >> 2) * (128u * 128u) + (uint32_t)(kk & 3) * 32u;
           const uint32_t boff = (uint32_t)(kk >> 2) * KM_HALF + (uint32_t)(kk & 3) * 32u;
-          const uint64_t ad = sdesc_sw128(base + OFF_SA + aoff, 16, 1024);
-          umma_ss(tmem + TM_VN, ad, sdesc_sw128(sb + ST_W + boff, 16, 1024), ID_N64, kk > 0 ? 1u : 0u);
-          umma_ss(tmem + TM_O, ad, sdesc_sw128(sb + ST_QG + boff, 16, 1024), ID_N64, kk > 0 ? 1u : 0u);
+          umma_ss(tmem + TM_VN, sdesc_sw128(base + OFF_SA + aoff, 16, 1024), sdesc_sw128(sb + ST_W + boff, 16, 1024),
+                  ID_N64, kk > 0 ? 1u : 0u);
         }
         umma_commit(bar0 + 8 * B_VN);
-        if (!mbar_wait(bar0 + 8 * B_VNEW, c & 1, abort_flag)) break;
+        // o^T = S^T Qg^T
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t aoff = (uint32_t)(kk >> 2) * (128u * 128u) + (uint32_t)(kk & 3) * 32u;
+          const uint32_t boff = (uint32_t)(kk >> 2) * KM_HALF + (uint32_t)(kk & 3) * 32u;
+          umma_ss(tO, sdesc_sw128(base + OFF_SA + aoff, 16, 1024), sdesc_sw128(sb + ST_QG + boff, 16, 1024), ID_N64,
+                  kk > 0 ? 1u : 0u);
+        }
+        if (!mbar_wait(bar0 + 8 * B_VNEW, n & 1, abort_flag)) break;
         tc_fence_after();
         // S^T += v_new^T Kg  (Kg MN-major: [2 dk halves][64 tok][128 B]; K = 64 tokens in 4 steps)
+#pragma unroll
+        for (int kt = 0; kt < 4; ++kt)
+          umma_ss(tmem + TM_S, sdesc_sw128(base + OFF_VA + kt * 32, 16, 1024),
+                  sdesc_sw128(sb + ST_KG + kt * 2048, KM_HALF, 1024), ID_N128_BMN, 1u);
+        umma_commit(bar0 + 8 * B_SDONE);
         // o^T += v_new^T Aqk^T
 #pragma unroll
-        for (int kt = 0; kt < 4; ++kt) {
-          const uint64_t ad = sdesc_sw128(base + OFF_VA + kt * 32, 16, 1024);
-          umma_ss(tmem + TM_S, ad, sdesc_sw128(sb + ST_KG + kt * 2048, KM_HALF, 1024), ID_N128_BMN, 1u);
-          umma_ss(tmem + TM_O, ad, sdesc_sw128(sb + ST_A + kt * 32, 16, 1024), ID_N64, 1u);
-        }
-        umma_commit(bar0 + 8 * B_SDONE);
+        for (int kt = 0; kt < 4; ++kt)
+          umma_ss(tO, sdesc_sw128(base + OFF_VA + kt * 32, 16, 1024), sdesc_sw128(sb + ST_A + kt * 32, 16, 1024),
+                  ID_N64, 1u);
+        umma_commit(bar0 + 8 * (B_ODONE0 + st));
         umma_commit(bar0 + 8 * (B_EMPTY0 + st));
       }
       // every MMA issued above has completed before TMEM is freed
@@ -520,33 +568,21 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
     const int r = q4 * 32 + lane;  // dv row == TMEM lane
     const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
     const uint32_t tS = tmem + lane_addr + TM_S, tVN = tmem + lane_addr + TM_VN, tO = tmem + lane_addr + TM_O;
-    const int64_t sh = (int64_t)s * H + h;
     uint8_t* sa = gbase + OFF_SA;
     uint8_t* va = gbase + OFF_VA;
     bf16* ost = reinterpret_cast<bf16*>(gbase + OFF_OST) + q4 * (64 * 32);  // [64 tok][32 dv] of this warp
 
-    // S^T[r][dk] = initial_state[dk][r]
-#pragma unroll
-    for (int cb = 0; cb < 4; ++cb) {
-      uint32_t v[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i)
-        v[i] = __float_as_uint(p.init_state ? p.init_state[(sh * DR_D + cb * 32 + i) * DR_D + r] : 0.f);
-      tmem_st32(tS + cb * 32, v);
-    }
-    tmem_st_wait();
-
-    // o^T of chunk c (complete in TMEM) -> out[token][h][dv], 64-byte pieces per token
-    auto o_epilogue = [&](int c) {
+    // o^T of chunk (s, h, c) (complete in TMEM buffer b) -> out[token][h][dv], 64-byte pieces
+    auto o_epilogue = [&](int b, int s, int h, int c) {
       uint32_t o[2][32];
-      tmem_ld32(tO, o[0]);
-      tmem_ld32(tO + 32, o[1]);
+      tmem_ld32(tO + 64 * b, o[0]);
+      tmem_ld32(tO + 64 * b + 32, o[1]);
       tmem_ld_wait();
 #pragma unroll
       for (int t = 0; t < 64; ++t) ost[t * 32 + lane] = __float2bfloat16_rn(__uint_as_float(o[t >> 5][t & 31]));
       __syncwarp();
-      const int tok0 = seg_t0 + c * DR_C;
-      const int len = min(DR_C, seg_len - c * DR_C);
+      const int tok0 = p.cu[s] + c * DR_C;
+      const int len = min(DR_C, p.cu[s + 1] - tok0);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int e = lane + i * 32, tr = e >> 2, ch = e & 3;
@@ -556,28 +592,50 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
       }
       __syncwarp();
     };
-    auto load_u = [&](int c, uint4 (&u)[8], float& g) {
-      const uint8_t* tile = p.tiles + ((size_t)(c0 + c) * H + h) * CH_BYTES;
-      const uint4* row = reinterpret_cast<const uint4*>(tile + OFF_UT + (size_t)r * DR_C * 2);
+    auto write_final = [&](int s, int h) {
+      if (!p.final_state) return;
+      const int64_t sh = (int64_t)s * H + h;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) u[i] = __ldg(row + i);
-      g = __ldg(reinterpret_cast<const float*>(tile + OFF_GAMMA));
+      for (int cb = 0; cb < 4; ++cb) {
+        uint32_t v[32];
+        tmem_ld32(tS + cb * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) p.final_state[(sh * DR_D + cb * 32 + i) * DR_D + r] = __uint_as_float(v[i]);
+      }
     };
 
-    bool ok = true;
-    uint4 ut[8];  // U^T row r of the current chunk, and gamma; prefetched one chunk ahead
-    float gam = 1.f;
-    if (nch > 0) load_u(0, ut, gam);
-    for (int c = 0; c < nch; ++c) {
-      if (c > 0) {
-        if (!warp_wait(bar0 + 8 * B_SDONE, (c - 1) & 1, abort_flag)) { ok = false; break; }
+    int ps = -1, ph = 0, pc = 0;  // the previous chunk (its output is written one chunk late)
+    for (int n = 0;; ++n) {
+      const int st = n & 1;
+      if (!warp_wait(bar0 + 8 * (B_FULL0 + st), (n >> 1) & 1, abort_flag)) break;
+      const int s = meta[st].s, h = meta[st].h, c = meta[st].c;
+      const float gam = meta[st].gamma;
+      if (n > 0) {  // S^T of the previous chunk is complete
+        if (!warp_wait(bar0 + 8 * B_SDONE, (n - 1) & 1, abort_flag)) break;
         tc_fence_after();
-        o_epilogue(c - 1);
       }
-      uint4 ut_next[8];
-      float gam_next = 1.f;
-      if (c + 1 < nch) load_u(c + 1, ut_next, gam_next);
-      // S^T -> bf16 A tile; S^T *= gamma_c in TMEM (the MMAs of this chunk read the A tile)
+      if (s < 0 || c == 0) {  // chain boundary
+        if (ps >= 0) write_final(ps, ph);
+        if (s < 0) {  // closing stage: output of the last chunk, then done
+          if (ps >= 0 && warp_wait(bar0 + 8 * (B_ODONE0 + (st ^ 1)), ((n - 1) >> 1) & 1, abort_flag)) {
+            tc_fence_after();
+            o_epilogue(st ^ 1, ps, ph, pc);
+          }
+          break;
+        }
+        const int64_t sh = (int64_t)s * H + h;
+#pragma unroll
+        for (int cb = 0; cb < 4; ++cb) {  // S^T[r][dk] = initial_state[dk][r]
+          uint32_t v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            v[i] = __float_as_uint(p.init_state ? p.init_state[(sh * DR_D + cb * 32 + i) * DR_D + r] : 0.f);
+          tmem_st32(tS + cb * 32, v);
+        }
+        tmem_st_wait();
+      }
+      // S^T -> bf16 A tile; S^T *= gamma in TMEM (this chunk's MMAs read the A tile)
 #pragma unroll
       for (int cb = 0; cb < 4; ++cb) {
         uint32_t v[32];
@@ -599,9 +657,10 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
       tc_fence_before();
       mbar_arrive(bar0 + 8 * B_SA);
       // v_new^T = U^T - vn -> bf16 A tile
-      if (!warp_wait(bar0 + 8 * B_VN, c & 1, abort_flag)) { ok = false; break; }
+      if (!warp_wait(bar0 + 8 * B_VN, n & 1, abort_flag)) break;
       tc_fence_after();
       {
+        const uint8_t* ut = gbase + st * ST_BYTES + ST_UT;
         uint32_t v[2][32];
         tmem_ld32(tVN, v[0]);
         tmem_ld32(tVN + 32, v[1]);
@@ -609,7 +668,7 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           float u[8], f[8];
-          unpack8(ut[j], u);
+          unpack8(*reinterpret_cast<const uint4*>(ut + sw128_off(r, j, 128)), u);
 #pragma unroll
           for (int i = 0; i < 8; ++i) f[i] = u[i] - __uint_as_float(v[j >> 2][(j & 3) * 8 + i]);
           *reinterpret_cast<uint4*>(va + sw128_off(r, j, 128)) = pack8(f);
@@ -618,28 +677,15 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(bar0 + 8 * B_VNEW);
-      if (c + 1 < nch) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) ut[i] = ut_next[i];
-        gam = gam_next;
-      }
-    }
-    if (ok && nch > 0) {
-      ok = warp_wait(bar0 + 8 * B_SDONE, (nch - 1) & 1, abort_flag);
-      if (ok) {
+      // output of the previous chunk (its o^T buffer is reused by the next chunk's MMAs)
+      if (ps >= 0) {
+        if (!warp_wait(bar0 + 8 * (B_ODONE0 + (st ^ 1)), ((n - 1) >> 1) & 1, abort_flag)) break;
         tc_fence_after();
-        o_epilogue(nch - 1);
+        o_epilogue(st ^ 1, ps, ph, pc);
       }
-    }
-    if (ok && p.final_state) {
-#pragma unroll
-      for (int cb = 0; cb < 4; ++cb) {
-        uint32_t v[32];
-        tmem_ld32(tS + cb * 32, v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) p.final_state[(sh * DR_D + cb * 32 + i) * DR_D + r] = __uint_as_float(v[i]);
-      }
+      ps = s;
+      ph = h;
+      pc = c;
     }
   }
   __syncwarp();
@@ -650,6 +696,18 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
     tmem_dealloc(tmem, TM_COLS);
   }
   if (tid == 0 && *abort_flag) atomicExch(&g_recur_error, 1);
+}
+
+// Final state of empty segments (their chains never enter the recurrence): the initial state, or 0.
+__global__ void empty_state_kernel(const int32_t* __restrict__ table, int heads, const float* __restrict__ init,
+                                   float* __restrict__ fin) {
+  const int s = blockIdx.x, h = blockIdx.y;
+  if (table[s + 1] > table[s]) return;
+  const int64_t off = ((int64_t)s * heads + h) * DR_D * DR_D;
+  for (int e = threadIdx.x * 4; e < DR_D * DR_D; e += blockDim.x * 4) {
+    float4 v = init ? *reinterpret_cast<const float4*>(init + off + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+    *reinterpret_cast<float4*>(fin + off + e) = v;
+  }
 }
 
 using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
@@ -667,14 +725,14 @@ static EncodeFn encode_fn() {
   return fn;
 }
 
-// 3-D map over one operand of every workspace tile: [n_tiles][64 rows][cols] bf16, tile stride
-// CH_BYTES, box 64 x 64 x 1, 128-byte swizzle.
-static int tile_map(CUtensorMap* m, const uint8_t* tiles, size_t off, int cols, int64_t n_tiles) {
+// 3-D map over one operand of every workspace tile: [n_tiles][rows][cols] bf16, tile stride
+// CH_BYTES, box 64 x rows x 1, 128-byte swizzle.
+static int tile_map(CUtensorMap* m, const uint8_t* tiles, size_t off, int cols, int rows, int64_t n_tiles) {
   EncodeFn enc = encode_fn();
   if (!enc) return set_error(FDK_ERR_DEVICE, "chunk_gated_delta_rule: cuTensorMapEncodeTiled unavailable");
-  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)DR_C, (cuuint64_t)n_tiles};
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)n_tiles};
   cuuint64_t strides[2] = {(cuuint64_t)cols * 2, (cuuint64_t)CH_BYTES};
-  cuuint32_t box[3] = {64, 64, 1};
+  cuuint32_t box[3] = {64, (cuuint32_t)rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<uint8_t*>(tiles + off), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -700,14 +758,19 @@ int delta_take_device_error() {
 }
 
 static int launch_recur(int nseg, int heads, int64_t n_tiles, cudaStream_t s, const int32_t* cu, const int32_t* table,
-                        const uint8_t* tiles, const float* init, bf16* out, float* fin) {
+                        int32_t* counter, const uint8_t* tiles, const float* init, bf16* out, float* fin) {
   using namespace drtc;
-  CUtensorMap mw, mqg, mkg, ma;
-  if (int st = tile_map(&mw, tiles, OFF_W, DR_D, n_tiles)) return st;
-  if (int st = tile_map(&mqg, tiles, OFF_QG, DR_D, n_tiles)) return st;
-  if (int st = tile_map(&mkg, tiles, OFF_KG, DR_D, n_tiles)) return st;
-  if (int st = tile_map(&ma, tiles, OFF_A, DR_C, n_tiles)) return st;
-  const RParams prm{cu, table, heads, tiles, init, out, fin};
+  if (fin) {
+    empty_state_kernel<<<dim3((unsigned)nseg, (unsigned)heads), 256, 0, s>>>(table, heads, init, fin);
+    if (int st = check_launch("chunk_gated_delta_rule/empty segments")) return st;
+  }
+  CUtensorMap mw, mqg, mkg, ma, mut;
+  if (int st = tile_map(&mw, tiles, OFF_W, DR_D, DR_C, n_tiles)) return st;
+  if (int st = tile_map(&mqg, tiles, OFF_QG, DR_D, DR_C, n_tiles)) return st;
+  if (int st = tile_map(&mkg, tiles, OFF_KG, DR_D, DR_C, n_tiles)) return st;
+  if (int st = tile_map(&ma, tiles, OFF_A, DR_C, DR_C, n_tiles)) return st;
+  if (int st = tile_map(&mut, tiles, OFF_UT, DR_C, DR_D, n_tiles)) return st;
+  const RParams prm{cu, table, counter, nseg, heads, tiles, init, out, fin};
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -715,7 +778,9 @@ static int launch_recur(int nseg, int heads, int64_t n_tiles, cudaStream_t s, co
     cudaFuncSetAttribute(delta_recur_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  delta_recur_tc_kernel<<<dim3((unsigned)nseg, (unsigned)heads), THREADS, SMEM_BYTES, s>>>(mw, mqg, mkg, ma, prm);
+  const int64_t items = (int64_t)nseg * heads;
+  const unsigned grid = (unsigned)(items < sm_count() ? items : sm_count());
+  delta_recur_tc_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(mw, mqg, mkg, ma, mut, prm);
   return check_launch("chunk_gated_delta_rule/recurrence");
 }
 
@@ -771,8 +836,8 @@ extern "C" int fdk_chunk_gated_delta_rule_fwd(const void* q, const void* k, int6
         static_cast<const bf16*>(beta), cu_seqlens, nseg, table, (int)heads, scale, tiles);
     if (int st = check_launch("chunk_gated_delta_rule/prep")) return st;
   }
-  return launch_recur(nseg, (int)heads, lay.max_chunks * heads, s, cu_seqlens, table, tiles, initial_state,
-                      static_cast<bf16*>(out), final_state);
+  return launch_recur(nseg, (int)heads, lay.max_chunks * heads, s, cu_seqlens, table, table + nseg + 1, tiles,
+                      initial_state, static_cast<bf16*>(out), final_state);
 }
 
 // ---------------------------------------------------------------------------------------------

@@ -143,85 +143,109 @@ __global__ void __launch_bounds__(256) gated_rmsnorm_kernel(
   const float inv = rsqrtf(ss * (1.0f / 128.0f) + eps);
   float r[8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) r[j] = wv[j] * (ov[j] * inv) * silu(zv[j]);
+  for (int j = 0; j < 8; ++j) r[j] = wv[j] * (ov[j] * inv) * silu_tanh(zv[j]);
   *reinterpret_cast<uint4*>(out + row * 128 + lane * 8) = pack8(r);
 }
 
 // ---------------------------------------------------------------------------------------------
-// q/k RMSNorm (1 + w) over head_dim + partial rotary embedding.  One warp per (token, head) row;
-// lane l holds features [l*E, l*E + E) with E = head_dim / 32 (4 for 128, 8 for 256).
+// q/k RMSNorm (1 + w) over head_dim + partial rotary embedding.  One warp per token: it walks the
+// token's hq + hkv head rows, four at a time with all four rows' loads issued first.  Lane l holds
+// features [l*E, l*E + E) of every row (E = head_dim / 32: 4 for 128, 8 for 256), so its norm
+// weights, cos / sin factors and rotate_half partner lane are loaded and computed once per token.
 // rotate_half pairs feature i with i + rot/2 inside the first rot features.
 // ---------------------------------------------------------------------------------------------
+template <int E>
+struct RowVec;
+template <>
+struct RowVec<4> {
+  uint2 u;
+  __device__ __forceinline__ void load(const bf16* p) { u = *reinterpret_cast<const uint2*>(p); }
+  __device__ __forceinline__ void to_float(float (&f)[4]) const {
+    float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+    float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
+  }
+  __device__ __forceinline__ static void store(bf16* p, const float (&f)[4]) {
+    uint2 o;
+    o.x = pack_bf16x2(f[0], f[1]);
+    o.y = pack_bf16x2(f[2], f[3]);
+    *reinterpret_cast<uint2*>(p) = o;
+  }
+};
+template <>
+struct RowVec<8> {
+  uint4 u;
+  __device__ __forceinline__ void load(const bf16* p) { u = *reinterpret_cast<const uint4*>(p); }
+  __device__ __forceinline__ void to_float(float (&f)[8]) const { unpack8(u, f); }
+  __device__ __forceinline__ static void store(bf16* p, const float (&f)[8]) { *reinterpret_cast<uint4*>(p) = pack8(f); }
+};
+
 template <int E, bool W_FP32>
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
     const bf16* __restrict__ qkv, int64_t ldq, const void* __restrict__ qw, const void* __restrict__ kw,
     const int32_t* __restrict__ pos, const float* __restrict__ rope, int max_pos, int rot, bf16* __restrict__ qo,
     bf16* __restrict__ ko, int64_t tokens, int hq, int hkv, float eps) {
   constexpr int D = E * 32;
-  const int64_t gw = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  constexpr int G = 4;  // rows in flight per warp
+  const int64_t t = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  const int64_t rows_per_tok = hq + hkv;
-  if (gw >= tokens * rows_per_tok) return;
-  const int64_t t = gw / rows_per_tok;
-  const int r = (int)(gw - t * rows_per_tok);
-  const bool is_q = r < hq;
-  const bf16* src = is_q ? qkv + t * ldq + (int64_t)r * 2 * D : qkv + t * ldq + (int64_t)hq * 2 * D + (int64_t)(r - hq) * D;
-  bf16* dst = is_q ? qo + (t * hq + r) * D : ko + (t * hkv + (r - hq)) * D;
-  const void* w = is_q ? qw : kw;
-  float x[E];
-  if (E == 4) {
-    uint2 u = *reinterpret_cast<const uint2*>(src + lane * 4);
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-    float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
-    x[0] = a.x; x[1] = a.y; x[2] = b.x; x[3] = b.y;
-  } else {
-    float tmp[8];
-    unpack8(*reinterpret_cast<const uint4*>(src + lane * 8), tmp);
-#pragma unroll
-    for (int j = 0; j < E; ++j) x[j] = tmp[j];
-  }
-  float ss = 0.f;
-#pragma unroll
-  for (int j = 0; j < E; ++j) ss = fmaf(x[j], x[j], ss);
-  ss = warp_sum(ss);
-  const float inv = rsqrtf(ss / (float)D + eps);
-#pragma unroll
-  for (int j = 0; j < E; ++j) {
-    const int f = lane * E + j;
-    float wf = W_FP32 ? __ldg(static_cast<const float*>(w) + f) : __bfloat162float(static_cast<const bf16*>(w)[f]);
-    x[j] = x[j] * inv * (1.0f + wf);
-  }
-  // partner lane holding feature f +/- rot/2 (rot/2 is a multiple of E since rot % 8 == 0 and E <= 8)
-  const int half = rot >> 1;
-  const int lane_off = half / E;
+  if (t >= tokens) return;
+  // per-lane constants of this token
+  float wq[E], wk[E], cf[E], sf[E];
+  int partner[E];
   int p = pos[t];
   p = p < 0 ? 0 : (p >= max_pos ? max_pos - 1 : p);   // callers guarantee 0 <= pos < max_pos
   const float* cs = rope + (int64_t)p * rot;            // cos[0:half] then sin[0:half]
-  float y[E];
+  const int half = rot >> 1;
+  const int lane_off = half / E;                        // rot/2 is a multiple of E (rot % 8 == 0, E <= 8)
 #pragma unroll
   for (int j = 0; j < E; ++j) {
     const int f = lane * E + j;
-    const int src_lane = (f < half) ? lane + lane_off : lane - lane_off;
-    float partner = __shfl_sync(0xffffffffu, x[j], src_lane < 0 ? 0 : (src_lane > 31 ? 31 : src_lane));
+    wq[j] = 1.0f + (W_FP32 ? __ldg(static_cast<const float*>(qw) + f) : __bfloat162float(static_cast<const bf16*>(qw)[f]));
+    wk[j] = 1.0f + (W_FP32 ? __ldg(static_cast<const float*>(kw) + f) : __bfloat162float(static_cast<const bf16*>(kw)[f]));
     if (f < rot) {
-      const float c = __ldg(cs + (f % half)), sn = __ldg(cs + half + (f % half));
-      const float rotv = (f < half) ? -partner : partner;
-      y[j] = x[j] * c + rotv * sn;
+      const int i = f < half ? f : f - half;
+      cf[j] = __ldg(cs + i);
+      sf[j] = f < half ? -__ldg(cs + half + i) : __ldg(cs + half + i);
+      partner[j] = f < half ? lane + lane_off : lane - lane_off;
     } else {
-      y[j] = x[j];
+      cf[j] = 1.f;
+      sf[j] = 0.f;
+      partner[j] = lane;
     }
   }
-  if (E == 4) {
-    uint2 u;
-    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
-    h[0] = __floats2bfloat162_rn(y[0], y[1]);
-    h[1] = __floats2bfloat162_rn(y[2], y[3]);
-    *reinterpret_cast<uint2*>(dst + lane * 4) = u;
-  } else {
-    float tmp[8];
+  const bf16* row0 = qkv + t * ldq;
+  const int nrows = hq + hkv;
+  for (int r0 = 0; r0 < nrows; r0 += G) {
+    RowVec<E> in[G];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) tmp[j] = y[j % E];
-    *reinterpret_cast<uint4*>(dst + lane * 8) = pack8(tmp);
+    for (int g = 0; g < G; ++g) {
+      const int r = r0 + g;
+      if (r < nrows) in[g].load(row0 + (r < hq ? (int64_t)r * 2 * D : (int64_t)hq * 2 * D + (int64_t)(r - hq) * D) + lane * E);
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const int r = r0 + g;
+      if (r >= nrows) break;  // warp-uniform
+      float x[E];
+      in[g].to_float(x);
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < E; ++j) ss = fmaf(x[j], x[j], ss);
+      ss = warp_sum(ss);
+      const float inv = rsqrtf(ss / (float)D + eps);
+      const bool is_q = r < hq;
+#pragma unroll
+      for (int j = 0; j < E; ++j) x[j] = x[j] * inv * (is_q ? wq[j] : wk[j]);
+      float y[E];
+#pragma unroll
+      for (int j = 0; j < E; ++j) {
+        const float other = __shfl_sync(0xffffffffu, x[j], partner[j]);
+        y[j] = fmaf(x[j], cf[j], other * sf[j]);
+      }
+      bf16* dst = is_q ? qo + (t * hq + r) * D : ko + (t * hkv + (r - hq)) * D;
+      RowVec<E>::store(dst + lane * E, y);
+    }
   }
 }
 
@@ -295,9 +319,9 @@ extern "C" int fdk_attn_qk_norm_rope(const void* qkv, int64_t ld_qkv, const void
     return set_error(FDK_ERR_INVALID_ARGUMENT, "attn_qk_norm_rope: bad sizes");
   if (!aligned16(qkv) || ld_qkv % 8 || !aligned16(q_out) || !aligned16(k_out))
     return set_error(FDK_ERR_ALIGNMENT, "attn_qk_norm_rope: pointers and strides must be 16-byte aligned");
-  const int64_t rows = tokens * (hq + hkv);
-  if (rows == 0) return FDK_OK;
-  dim3 grid((unsigned)((rows + 7) / 8));
+  if (tokens == 0) return FDK_OK;
+  if ((tokens + 7) / 8 > 0x7fffffff) return set_error(FDK_ERR_UNSUPPORTED, "attn_qk_norm_rope: too many tokens");
+  dim3 grid((unsigned)((tokens + 7) / 8));  // one warp per token
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto in = static_cast<const bf16*>(qkv);
   auto qo = static_cast<bf16*>(q_out);

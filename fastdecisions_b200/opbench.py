@@ -1,0 +1,147 @@
+"""Per-op timing of the decision forward's device ops on one packed config-5 batch.
+
+``python -m fastdecisions_b200.opbench --op delta_rule --batch 0`` builds batch ``--batch`` of the
+config-5 plan (256 seeded requests, longest-first packing into 32768-token batches), runs one op on
+layer-shaped synthetic inputs (seeded), and prints one JSON line per op: CUDA-event time per call,
+the algorithmic work of one call and the fraction of the measured peak in MEASURED_PEAKS.json.
+This is the small, self-contained case used for kernel profiles (one op, a few hundred MB on the
+device); ``bench.py`` is the end-to-end measurement.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import numpy as np
+import torch
+
+from . import ops
+from .engine import plan_batches
+from .workloads import ModelConfig, config5_requests
+
+OPS = ("delta_rule", "gqa_attention", "packed_conv", "qk_norm_rope", "gated_rmsnorm", "residual_rmsnorm", "swiglu",
+       "gdn_gates")
+
+
+def _peaks() -> dict:
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm": float(d["hbm_gbs"]), "tensor": float(d["bf16_tflops"]), "source": "measured (burst)"}
+    except (OSError, KeyError, ValueError):
+        return {"hbm": 6650.0, "tensor": 1590.0, "source": "fallback"}
+
+
+def batch_lengths(index: int, requests: int = 256, max_tokens: int = 32768) -> list:
+    lens = [r.ids.size for r in config5_requests(requests)]
+    plan = plan_batches(lens, max_tokens)
+    return [lens[i] for i in plan[index]]
+
+
+def make_case(op: str, lens: list, cfg: ModelConfig, seed: int = 0):
+    """Returns (callable, ("tensor", flops) | ("hbm", bytes)) for one call of ``op``."""
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    dev = "cuda"
+    T = int(sum(lens))
+    L = np.asarray(lens, dtype=np.int64)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(L)]), dtype=torch.int32, device=dev)
+    pos = torch.cat([torch.arange(n, dtype=torch.int32) for n in lens]).to(dev)
+
+    def rn(*shape, scale=1.0):
+        return (scale * torch.randn(*shape, generator=g, device=dev)).bfloat16()
+
+    Hk, Hv, Dk, Dv = cfg.linear_num_key_heads, cfg.linear_num_value_heads, cfg.linear_key_head_dim, \
+        cfg.linear_value_head_dim
+    kd, vd = Hk * Dk, Hv * Dv
+    C = 2 * kd + vd
+    hq, hkv, D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+    if op == "delta_rule":
+        q, k, v = rn(1, T, Hk, Dk), rn(1, T, Hk, Dk), rn(1, T, Hv, Dv, scale=0.5)
+        gg = -torch.rand(1, T, Hv, generator=g, device=dev) * 0.5
+        beta = torch.rand(1, T, Hv, generator=g, device=dev).bfloat16()
+        ws = torch.empty(ops.delta_rule_workspace_bytes(T, len(lens), Hv), dtype=torch.uint8, device=dev)
+        fn = lambda: ops.chunk_gated_delta_rule(q, k, v, gg, beta, cu_seqlens=cu, workspace=ws)  # noqa: E731
+        return fn, ("tensor", Hv * float(np.ceil(L / 64).sum()) * 11.7e6)
+    if op == "gqa_attention":
+        q, k, v = rn(T, hq, D), rn(T, hkv, D), rn(T, hkv, D)
+        fn = lambda: ops.gqa_attention_varlen_(q, k, v, cu, int(L.max()))  # noqa: E731
+        return fn, ("tensor", 2.0 * hq * D * float((L * (L + 1)).sum()))
+    if op == "packed_conv":
+        x = rn(1, T, C)
+        w = rn(C, cfg.linear_conv_kernel_dim, scale=0.3)
+        fn = lambda: ops.packed_conv_qkv(x, w, kd, vd, Dk, cu)  # noqa: E731
+        return fn, ("hbm", T * C * 2.0 * 2)
+    if op == "qk_norm_rope":
+        proj = rn(T, (2 * hq + 2 * hkv) * D)
+        qn, kn = rn(D, scale=0.02), rn(D, scale=0.02)
+        rope = ops.rope_table(ops.rope_inv_freq(D, cfg.partial_rotary_factor, cfg.rope_theta).to(dev), int(L.max()))
+        fn = lambda: ops.attn_qk_norm_rope(proj, qn, kn, pos, rope, hq, hkv, D, cfg.rms_norm_eps)  # noqa: E731
+        return fn, ("hbm", T * (hq + hkv) * D * 2.0 * 2)
+    if op == "gated_rmsnorm":
+        o, z = rn(T, Hv, Dv), rn(T, vd)
+        w = rn(Dv, scale=0.1) + 1.0
+        fn = lambda: ops.gated_rmsnorm(o, z, w, cfg.rms_norm_eps)  # noqa: E731
+        return fn, ("hbm", T * vd * 6.0)
+    if op == "residual_rmsnorm":
+        H = cfg.hidden_size
+        x = rn(T, H)
+        h = torch.randn(T, H, generator=g, device=dev)
+        w = rn(H, scale=0.02)
+        fn = lambda: ops.residual_rmsnorm(x, h, w, cfg.rms_norm_eps, residual_out=h)  # noqa: E731
+        return fn, ("hbm", T * H * (2 + 4 + 4 + 2.0))
+    if op == "swiglu":
+        I = cfg.intermediate_size
+        gu = rn(T, 2 * I)
+        fn = lambda: ops.swiglu(gu, I)  # noqa: E731
+        return fn, ("hbm", T * I * 6.0)
+    if op == "gdn_gates":
+        a, b = rn(T, Hv), rn(T, Hv)
+        A_log = torch.log(torch.empty(Hv, device=dev).uniform_(1, 16))
+        dt = torch.ones(Hv, device=dev)
+        fn = lambda: ops.gdn_gates(a, b, A_log, dt)  # noqa: E731
+        return fn, ("hbm", T * Hv * 10.0)
+    raise ValueError(f"unknown op {op!r}")
+
+
+def time_op(fn, iters: int, warmup: int) -> float:
+    """Mean milliseconds per call (CUDA events on the current stream, L2 flushed between calls)."""
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    total = 0.0
+    for _ in range(iters):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        e1.synchronize()
+        total += e0.elapsed_time(e1)
+    return total / iters
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--op", default="all", help="one of %s, or all" % ", ".join(OPS))
+    ap.add_argument("--batch", type=int, default=0, help="index into the config-5 batch plan")
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    args = ap.parse_args(argv)
+    cfg = ModelConfig()
+    lens = batch_lengths(args.batch)
+    peaks = _peaks()
+    for op in (OPS if args.op == "all" else (args.op,)):
+        fn, (bound, work) = make_case(op, lens, cfg)
+        ms = time_op(fn, args.iters, args.warmup)
+        achieved = work / (ms * 1e-3) / (1e12 if bound == "tensor" else 1e9)
+        print(json.dumps({"op": op, "batch": args.batch, "tokens": int(sum(lens)), "segments": len(lens),
+                          "max_len": int(max(lens)), "us": round(ms * 1e3, 2), "bound": bound,
+                          "achieved": round(achieved, 1), "unit": "TFLOP/s" if bound == "tensor" else "GB/s",
+                          "frac": round(achieved / peaks[bound], 4), "peak_source": peaks["source"]}), flush=True)
+
+
+if __name__ == "__main__":
+    main()
