@@ -1,22 +1,20 @@
 // Chunked gated delta rule (Gated DeltaNet core), chunk = 64 tokens, dk = dv = 128.
 //
 // Restates transformers' torch_chunk_gated_delta_rule (models/qwen3_5/modeling_qwen3_5.py:234-311)
-// for packed varlen input.  Three launches:
-//   1. chunk_table_kernel : per-segment chunk offsets (device side, graph-capturable).
-//   2. delta_prep_kernel  : one 256-thread CTA per (chunk, head), fully parallel.  l2-normalises q
-//      and k, takes the in-chunk cumsum G of the log decay, forms KK^T and QK^T on the tensor
-//      cores, inverts the unit-lower-triangular (I - L) in fp32 (16x16 diagonal blocks by forward
-//      substitution with each column held in registers, then block forward substitution), and
-//      writes into the caller's workspace (bf16)
-//        W  = T diag(beta e^G) K      Ut = (T diag(beta) V)^T       Aqk = (QK^T o decay), lower
-//        Qg = q e^G                   Kg = k e^(G_last - G)         gamma = e^G_last (fp32)
-//   3. delta_recur_kernel : one CTA per (segment, head, dv slice), sequential over the segment's
-//      chunks.  Each warp owns 16 dv rows of the TRANSPOSED state S^T [dv x dk] as fp32 mma
-//      accumulators and never exchanges data with other warps:
+// for packed varlen input.  Three launches (four with final states):
+//   1. chunk_table_kernel : per-segment chunk offsets and per-chunk (first token, length), device
+//      side and graph-capturable.
+//   2. delta_prep_kernel  : one 256-thread CTA per (chunk, head), fully parallel, three CTAs per
+//      SM.  TMA brings the raw q / k rows, the CTA l2-normalises them, takes the in-chunk cumsum G
+//      of the log decay, forms [K;Q] K^T as one M=128 tcgen05 MMA, inverts the unit-lower-
+//      triangular (I - L) in fp32 on the CUDA cores (16x16 diagonal blocks by forward
+//      substitution, then block forward substitution), and forms U^T and W^T as two more MMAs
+//      (V and K as MN-major A operands).  It writes into the caller's workspace (bf16)
+//        W^T = (T diag(beta e^G) K)^T   U^T = (T diag(beta) V)^T     Aqk = (QK^T o decay), lower
+//        Qg  = q e^G                    Kg  = k e^(G_last - G)       gamma = e^G_last (fp32)
+//   3. delta_recur_tc_kernel : persistent; each CTA takes (segment, head) chains from a work
+//      counter and runs them chunk by chunk with the state S^T [dv x dk] resident in TMEM:
 //        v_new^T = U^T - S^T W^T ;  o^T = S^T Qg^T + v_new^T Aqk^T ;  S^T = gamma S^T + v_new^T Kg
-//      An accumulator tile of one product is the A operand of the next (bf16-packed in
-//      registers), so the state never round-trips through shared memory; the chunk tiles stream
-//      in with cp.async, double-buffered, into XOR-swizzled (bank-conflict-free) shared memory.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -29,7 +27,8 @@ namespace fdk {
 constexpr int DR_C = 64;    // chunk length
 constexpr int DR_D = 128;   // dk == dv
 
-// Per (chunk, head) workspace tile: W, Qg, Kg [64][128], Ut [128][64], Aqk [64][64] (bf16), gamma.
+// Per (chunk, head) workspace tile: W^T [128][64], Qg, Kg [64][128], U^T [128][64], Aqk [64][64]
+// (bf16), gamma (fp32).
 constexpr size_t TILE128 = (size_t)DR_C * DR_D * 2;
 constexpr size_t TILE64 = (size_t)DR_C * DR_C * 2;
 constexpr size_t OFF_W = 0, OFF_QG = TILE128, OFF_KG = 2 * TILE128, OFF_UT = 3 * TILE128, OFF_A = 4 * TILE128,
@@ -39,225 +38,281 @@ constexpr size_t CH_BYTES = 4 * TILE128 + TILE64 + 16;
 __host__ __device__ inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 struct WsLayout {
-  size_t off_table, off_tiles, total;
+  size_t off_table, off_info, off_tiles, total;
   int64_t max_chunks;
 };
 
+// chunk table [nseg + 1] + work counter, chunk info (first token, length) [max_chunks], tiles
 __host__ __device__ inline WsLayout ws_layout(int64_t tokens, int64_t nseg, int64_t heads) {
   WsLayout l;
   l.max_chunks = (tokens + DR_C - 1) / DR_C + nseg;
   l.off_table = 0;
-  l.off_tiles = align256((size_t)(nseg + 2) * 4);  // chunk table [nseg + 1] + work counter
+  l.off_info = align256((size_t)(nseg + 2) * 4);
+  l.off_tiles = l.off_info + align256((size_t)l.max_chunks * 8);
   l.total = l.off_tiles + align256((size_t)l.max_chunks * heads * CH_BYTES);
   return l;
 }
 
-// XOR-swizzled row-major bf16 tiles: 16-byte chunk c of row r lives at chunk c ^ (r & 7).
-template <int COLS>
-__device__ __forceinline__ int swz(int r, int col) {
-  return r * COLS + ((((col >> 3) ^ (r & 7))) << 3) + (col & 7);
-}
-
-// ldmatrix fragment loads from swizzled tiles (same conventions as mma_sm80.cuh).
-template <int COLS>
-__device__ __forceinline__ void lda_sw(const __nv_bfloat16* t, int r0, int c0, uint32_t (&a)[4]) {
-  const int lane = threadIdx.x & 31;
-  ldsm_x4(smem_u32(t + swz<COLS>(r0 + (lane & 15), c0 + ((lane >> 4) << 3))), a[0], a[1], a[2], a[3]);
-}
-template <int COLS>  // B^T stored [n][k]
-__device__ __forceinline__ void ldb_nk_sw(const __nv_bfloat16* t, int n0, int k0, uint32_t (&b)[4]) {
-  const int lane = threadIdx.x & 31, m = lane >> 3;
-  ldsm_x4(smem_u32(t + swz<COLS>(n0 + (lane & 7) + ((m >> 1) << 3), k0 + ((m & 1) << 3))), b[0], b[1], b[2], b[3]);
-}
-template <int COLS>  // B stored [k][n]
-__device__ __forceinline__ void ldb_kn_sw(const __nv_bfloat16* t, int n0, int k0, uint32_t (&b)[4]) {
-  const int lane = threadIdx.x & 31, m = lane >> 3;
-  ldsm_x4_t(smem_u32(t + swz<COLS>(k0 + (lane & 7) + ((m & 1) << 3), n0 + ((m >> 1) << 3))), b[0], b[1], b[2], b[3]);
-}
-
-__device__ __forceinline__ void cp_async16_zfill(void* smem, const void* gmem, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(smem)), "l"(gmem), "r"(valid ? 16 : 0));
-}
-
-__global__ void chunk_table_kernel(const int32_t* __restrict__ cu, int nseg, int32_t* __restrict__ table) {
-  // single warp: exclusive scan of ceil(len / 64) over segments
-  const int lane = threadIdx.x;
+// One CTA of 256 threads: exclusive scan of ceil(len / 64) over segments (table[s] = first chunk
+// of segment s, table[nseg] = chunk count), each chunk's (first token, length), and the zeroed
+// work counter of the recurrence (table[nseg + 1]).
+__global__ void __launch_bounds__(256) chunk_table_kernel(const int32_t* __restrict__ cu, int nseg,
+                                                          int32_t* __restrict__ table, int2* __restrict__ info) {
+  __shared__ int warp_sums[8];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int carry = 0;
-  for (int base = 0; base < nseg; base += 32) {
-    const int s = base + lane;
-    int n = 0;
+  for (int base = 0; base < nseg; base += 256) {
+    const int s = base + tid;
+    int n = 0, t0 = 0, len = 0;
     if (s < nseg) {
-      const int len = cu[s + 1] - cu[s];
+      t0 = cu[s];
+      len = cu[s + 1] - t0;
       n = len > 0 ? (len + DR_C - 1) / DR_C : 0;
     }
     int incl = n;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      int y = __shfl_up_sync(0xffffffffu, incl, o);
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
       if (lane >= o) incl += y;
     }
-    if (s < nseg) table[s] = carry + incl - n;
-    carry += __shfl_sync(0xffffffffu, incl, 31);
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    int woff = 0, total = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      woff += w < warp ? warp_sums[w] : 0;
+      total += warp_sums[w];
+    }
+    const int first = carry + woff + incl - n;
+    if (s < nseg) {
+      table[s] = first;
+      for (int c = 0; c < n; ++c) info[first + c] = make_int2(t0 + c * DR_C, min(DR_C, len - c * DR_C));
+    }
+    carry += total;
+    __syncthreads();  // warp_sums is rewritten by the next pass
   }
-  if (lane == 0) {
+  if (tid == 0) {
     table[nseg] = carry;
     table[nseg + 1] = 0;  // work counter of the recurrence
   }
 }
 
+// byte offset of 16-byte chunk `c16` of row `r` in a [c16 / 8][rows][128 B] 128-byte-swizzled tile
+__device__ __forceinline__ uint32_t sw128_off(int r, int c16, int rows) {
+  return (uint32_t)(c16 >> 3) * (uint32_t)(rows * 128) + (uint32_t)r * 128u + ((uint32_t)((c16 & 7) ^ (r & 7)) << 4);
+}
+
+// warp-uniform bounded wait: every lane polls, the warp proceeds only if all lanes saw the phase
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  const bool ok = sm100::mbar_wait(bar, parity, abort_flag);
+  return __all_sync(0xffffffffu, ok ? 1 : 0) != 0;
+}
+
+__device__ int g_delta_error = 0;  // set when a bounded wait of a delta-rule kernel ran out
+
 // ------------------------------------------------------------------------------------------ prep
-constexpr int PREP_THREADS = 256;
-constexpr int LDF = DR_C + 4;     // fp32 tile stride: conflict-free column solves and row reads
-constexpr int UT_LD = DR_C + 8;   // padded row of the transposed U staging tile
+namespace dprep {
+using namespace sm100;
 
-struct PrepSmem {
-  __nv_bfloat16 q[DR_C * DR_D];   // swizzled; TU / TW (2 x [64][64]) after QK^T; W staging last
-  __nv_bfloat16 k[DR_C * DR_D];   // swizzled; with v: U^T staging [128][UT_LD] after U/W
-  __nv_bfloat16 v[DR_C * DR_D];   // swizzled
-  float L[DR_C][LDF];             // strictly lower L, then block-solve scratch
-  float T[DR_C][LDF];
-  float G[DR_C];
-  float beta[DR_C];
-  int info[2];
-};
+constexpr int THREADS = 256;
+constexpr int LDF = DR_C + 4;                 // fp32 tile stride: conflict-free column solves and row stores
+constexpr uint32_t A1 = 0;                    // [2 dk halves][128 rows][128 B]: rows 0-63 k^, 64-127 q^ then V
+constexpr uint32_t LF = 32768;                // fp32 L [64][LDF]; after the solve TU and TW (8 KB each)
+constexpr uint32_t TU_OFF = LF, TW_OFF = LF + 8192;
+constexpr uint32_t TF = LF + 64 * LDF * 4;    // fp32 T [64][LDF]
+constexpr uint32_t VEC = TF + 64 * LDF * 4;   // G * log2(e), beta, beta, beta e^G: [4][64] fp32
+constexpr uint32_t BARS = VEC + 4 * 64 * 4;
+enum { B_QK = 0, B_MMA1, B_V, B_MMA2, B_DRAIN, NBAR };
+constexpr uint32_t SMEM_BYTES = BARS + 8 * NBAR + 16 + 1024;
+constexpr uint32_t TM_D1 = 0, TM_U = 64, TM_W = 0, TM_COLS = 128;
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr long long DRAIN_BUDGET = 2000000000LL;
 
-__global__ void __launch_bounds__(PREP_THREADS, 2) delta_prep_kernel(
-    const bf16* __restrict__ q, const bf16* __restrict__ k, int64_t ldqk, const bf16* __restrict__ v, int64_t ldv,
-    const float* __restrict__ g, const bf16* __restrict__ beta, const int32_t* __restrict__ cu, int nseg,
-    const int32_t* __restrict__ table, int heads, float scale, uint8_t* __restrict__ tiles) {
-  extern __shared__ __align__(128) uint8_t smem_raw[];
-  PrepSmem& sm = *reinterpret_cast<PrepSmem*>(smem_raw);
-  const int ci = blockIdx.x;
-  const int h = blockIdx.y;
+__global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
+    const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
+    const __grid_constant__ CUtensorMap mv, const float* __restrict__ g, const bf16* __restrict__ beta,
+    const int2* __restrict__ info, const int32_t* __restrict__ table, int nseg, int heads, float scale,
+    uint8_t* __restrict__ tiles) {
+  extern __shared__ uint8_t smem_raw[];
+  const int ci = blockIdx.x, h = blockIdx.y;
+  if (ci >= table[nseg]) return;  // CTA-uniform, before any barrier or TMEM use
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* sb = smem_raw + (base - raw);
+  float* G2 = reinterpret_cast<float*>(sb + VEC);  // G * log2(e)
+  float* bet = G2 + 64;                            // beta (0 past the chunk's length)
+  float* fw = G2 + 128;                            // beta e^G
+  float* Lf = reinterpret_cast<float*>(sb + LF);
+  float* Tf = reinterpret_cast<float*>(sb + TF);
+  const uint32_t bar0 = base + BARS;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sb + BARS + 8 * NBAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sb + BARS + 8 * NBAR + 4);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int gq = lane >> 2, tq = lane & 3;
-  if (ci >= table[nseg]) return;
-  if (tid == 0) {
-    int lo = 0, hi = nseg - 1;  // largest segment s with table[s] <= ci (empty segments skipped)
-    while (lo < hi) {
-      int mid = (lo + hi + 1) >> 1;
-      if (table[mid] <= ci) lo = mid; else hi = mid - 1;
-    }
-    const int t0 = cu[lo] + (ci - table[lo]) * DR_C;
-    sm.info[0] = t0;
-    sm.info[1] = min(DR_C, cu[lo + 1] - t0);
-  }
-  __syncthreads();
-  const int t0 = sm.info[0], len = sm.info[1];
+  const int2 inf = info[ci];
+  const int t0 = inf.x, len = inf.y;
   uint8_t* tile = tiles + ((size_t)ci * heads + h) * CH_BYTES;
 
-  // 1. q, k, v rows -> swizzled smem (zero-filled past len); decay cumsum and beta
-  for (int e = tid; e < DR_C * 16; e += PREP_THREADS) {
-    const int r = e >> 4, c = (e & 15) << 3;
-    const bool ok = r < len;
-    const int64_t t = t0 + (ok ? r : 0);
-    cp_async16_zfill(&sm.q[swz<DR_D>(r, c)], q + t * ldqk + (int64_t)h * DR_D + c, ok);
-    cp_async16_zfill(&sm.k[swz<DR_D>(r, c)], k + t * ldqk + (int64_t)h * DR_D + c, ok);
-    cp_async16_zfill(&sm.v[swz<DR_D>(r, c)], v + t * ldv + (int64_t)h * DR_D + c, ok);
+  if (tid == 0) {
+    for (int i = 0; i < NBAR; ++i) mbar_init(bar0 + 8 * i, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
   }
-  cp_async_commit();
   if (warp == 0) {
-    float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+    tmem_alloc(smem_u32(tmem_slot), TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool issued_v = false, issued_mma = false;
+
+  // 1. raw k rows -> A1 rows 0-63, raw q rows -> rows 64-127 (TMA, 128-byte swizzle; rows past
+  //    the end of the tokens read as zero, rows of the next segment are masked below)
+  if (tid == 0) {
+    prefetch_tmap(&mq);
+    prefetch_tmap(&mk);
+    prefetch_tmap(&mv);
+    mbar_expect_tx(bar0 + 8 * B_QK, 4 * 8192);
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      tma_load_2d(base + A1 + hf * 16384, &mk, bar0 + 8 * B_QK, h * DR_D + hf * 64, t0);
+      tma_load_2d(base + A1 + hf * 16384 + 8192, &mq, bar0 + 8 * B_QK, h * DR_D + hf * 64, t0);
+    }
+  }
+  // decay cumsum (log2 domain), beta and the column factors of TU / TW
+  if (warp == 1) {
     const int r0 = 2 * lane, r1 = 2 * lane + 1;
+    float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
     if (r0 < len) { a0 = g[(int64_t)(t0 + r0) * heads + h]; b0 = __bfloat162float(beta[(int64_t)(t0 + r0) * heads + h]); }
     if (r1 < len) { a1 = g[(int64_t)(t0 + r1) * heads + h]; b1 = __bfloat162float(beta[(int64_t)(t0 + r1) * heads + h]); }
     const float pair = a0 + a1;
     float incl = pair;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      float y = __shfl_up_sync(0xffffffffu, incl, o);
+      const float y = __shfl_up_sync(0xffffffffu, incl, o);
       if (lane >= o) incl += y;
     }
-    const float excl = incl - pair;
-    sm.G[r0] = excl + a0;
-    sm.G[r1] = excl + a0 + a1;
-    sm.beta[r0] = b0;
-    sm.beta[r1] = b1;
+    const float G0 = incl - pair + a0, G1 = incl;  // natural-log cumsum at r0, r1
+    G2[r0] = G0 * LOG2E;
+    G2[r1] = G1 * LOG2E;
+    bet[r0] = b0;
+    bet[r1] = b1;
+    fw[r0] = b0 * expf(G0);
+    fw[r1] = b1 * expf(G1);
+    if (lane == 31) *reinterpret_cast<float*>(tile + OFF_GAMMA) = expf(G1);
   }
-  cp_async_wait<0>();
-  __syncthreads();
+  bool ok = mbar_wait(bar0 + 8 * B_QK, 0, abort_flag);
+  ok = __syncthreads_and(ok) != 0;  // also publishes G2 / beta / fw
 
-  // 2. l2 norm of q (times scale) and k rows in fp32; Qg = q e^G and Kg = k e^(G_last - G) out
-  {
-    const float glast = sm.G[DR_C - 1];
-    __nv_bfloat16* wsQg = reinterpret_cast<__nv_bfloat16*>(tile + OFF_QG);
-    __nv_bfloat16* wsKg = reinterpret_cast<__nv_bfloat16*>(tile + OFF_KG);
-    for (int rr = warp; rr < 2 * DR_C; rr += PREP_THREADS / 32) {
-      const bool isq = rr < DR_C;
-      const int r = isq ? rr : rr - DR_C;
-      __nv_bfloat16* row = isq ? sm.q : sm.k;
-      const int col = lane * 4;
-      uint2 u = *reinterpret_cast<const uint2*>(&row[swz<DR_D>(r, col)]);
-      float2 x01 = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u.x));
-      float2 x23 = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u.y));
-      float ss = x01.x * x01.x + x01.y * x01.y + x23.x * x23.x + x23.y * x23.y;
-      ss = warp_sum(ss);
-      const float inv = rsqrtf(ss + 1e-6f) * (isq ? scale : 1.0f);
-      x01.x *= inv; x01.y *= inv; x23.x *= inv; x23.y *= inv;
-      uint2 o;
-      o.x = pack_bf16x2(x01.x, x01.y);
-      o.y = pack_bf16x2(x23.x, x23.y);
-      *reinterpret_cast<uint2*>(&row[swz<DR_D>(r, col)]) = o;
-      // decayed copies use the bf16-rounded normalised values (what the products see)
-      const float2 n01 = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&o.x));
-      const float2 n23 = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&o.y));
-      const float f = isq ? expf(sm.G[r]) : expf(glast - sm.G[r]);
-      uint2 d;
-      d.x = pack_bf16x2(n01.x * f, n01.y * f);
-      d.y = pack_bf16x2(n23.x * f, n23.y * f);
-      *reinterpret_cast<uint2*>((isq ? wsQg : wsKg) + r * DR_D + col) = d;
-    }
-  }
-  __syncthreads();
-
-  // 3. KK^T and QK^T: warp w -> rows [16 (w%4), +16), cols [32 (w/4), +32); decay and masks
-  {
-    const int r0 = (warp & 3) * 16, n0 = (warp >> 2) * 32;
-    float kk[4][4], qk[4][4];
+  if (ok) {
+    // 2. l2-normalise k and q rows (q also times scale) in place, zero rows past the length;
+    //    decayed copies Kg = k e^(G_last - G), Qg = q e^G out (from the bf16-rounded normalised
+    //    values the products see).  Four threads per row, 32 features each.
+    const int row = tid >> 2, part = tid & 3;
+    const bool valid = row < len;
 #pragma unroll
-    for (int n = 0; n < 4; ++n)
+    for (int rr = 0; rr < 2; ++rr) {
+      const int srow = rr * 64 + row;
+      uint4 u[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) kk[n][j] = qk[n][j] = 0.f;
+      for (int j = 0; j < 4; ++j) u[j] = *reinterpret_cast<const uint4*>(sb + A1 + sw128_off(srow, part * 4 + j, 128));
+      float ss = 0.f;
 #pragma unroll
-    for (int ks = 0; ks < DR_D; ks += 16) {
-      uint32_t ak[4], aq[4];
-      lda_sw<DR_D>(sm.k, r0, ks, ak);
-      lda_sw<DR_D>(sm.q, r0, ks, aq);
+      for (int j = 0; j < 4; ++j) {
+        float f[8];
+        unpack8(u[j], f);
 #pragma unroll
-      for (int n = 0; n < 4; n += 2) {
-        uint32_t b[4];
-        ldb_nk_sw<DR_D>(sm.k, n0 + n * 8, ks, b);
-        mma_bf16_16816(kk[n], ak, b[0], b[1]);
-        mma_bf16_16816(kk[n + 1], ak, b[2], b[3]);
-        mma_bf16_16816(qk[n], aq, b[0], b[1]);
-        mma_bf16_16816(qk[n + 1], aq, b[2], b[3]);
+        for (int e = 0; e < 8; ++e) ss = fmaf(f[e], f[e], ss);
+      }
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+      const float inv = valid ? rsqrtf(ss + 1e-6f) * (rr ? scale : 1.0f) : 0.f;
+      const float dec = rr ? exp2f(G2[row]) : exp2f(G2[63] - G2[row]);
+      uint4* gout = reinterpret_cast<uint4*>(tile + (rr ? OFF_QG : OFF_KG) + (size_t)row * 256 + part * 64);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float f[8], d[8];
+        unpack8(u[j], f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] *= inv;
+        const uint4 nb = pack8(f);
+        *reinterpret_cast<uint4*>(sb + A1 + sw128_off(srow, part * 4 + j, 128)) = nb;
+        unpack8(nb, f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) d[e] = f[e] * dec;
+        gout[j] = pack8(d);
       }
     }
-    __nv_bfloat16* wsA = reinterpret_cast<__nv_bfloat16*>(tile + OFF_A);
+    fence_proxy_async_smem();
+  }
+  __syncthreads();
+
+  // 3. D1 = [K^; Q^] K^T  (M128 N64 K128; B is A's first 64 rows)
+  if (ok && tid == 0) {
+    tc_fence_after();
+    constexpr uint32_t ID = idesc_bf16(128, 64, false, false);
 #pragma unroll
-    for (int n = 0; n < 4; ++n)
+    for (int kk = 0; kk < 8; ++kk) {
+      const uint64_t d = sdesc_sw128(base + A1 + (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u, 16, 1024);
+      umma_ss(tmem + TM_D1, d, d, ID, kk > 0 ? 1u : 0u);
+    }
+    umma_commit(bar0 + 8 * B_MMA1);
+    issued_mma = true;
+  }
+  if (ok) ok = warp_wait(bar0 + 8 * B_MMA1, 0, abort_flag);
+  if (ok) tc_fence_after();
+  // V rows -> A1 rows 64-127 (q^ is no longer read), landing while the solve runs
+  if (ok && tid == 0) {
+    mbar_expect_tx(bar0 + 8 * B_V, 2 * 8192);
+    tma_load_2d(base + A1 + 8192, &mv, bar0 + 8 * B_V, h * DR_D, t0);
+    tma_load_2d(base + A1 + 16384 + 8192, &mv, bar0 + 8 * B_V, h * DR_D + 64, t0);
+    issued_v = true;
+  }
+
+  // 4. rows of D1: L = -beta_i (KK^T)_ij e^(G_i - G_j) (j < i) -> smem; Aqk = (QK^T)_ij e^(G_i - G_j)
+  //    (j <= i) -> workspace.  Warp w reads TMEM lane quarter w % 4, column half w / 4.
+  if (ok) {
+    const int q4 = warp & 3, chh = warp >> 2;
+    uint32_t v[32];
+    tmem_ld32(tmem + ((uint32_t)(q4 * 32) << 16) + TM_D1 + chh * 32, v);
+    tmem_ld_wait();
+    const int i = (q4 & 1) * 32 + lane;
+    const float g2i = G2[i];
+    if (q4 < 2) {
+      const float nb = -bet[i];
+      float* dst = Lf + i * LDF + chh * 32;
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int i = r0 + gq + hh * 8;
-        const int j0 = n0 + n * 8 + 2 * tq;
-        float l2[2], a2[2];
+      for (int j8 = 0; j8 < 4; ++j8) {
+        float l[8];
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int j = j0 + e;
-          const float dec = (i >= j) ? expf(sm.G[i] - sm.G[j]) : 0.f;
-          l2[e] = (i > j) ? -sm.beta[i] * kk[n][hh * 2 + e] * dec : 0.f;
-          a2[e] = (i >= j) ? qk[n][hh * 2 + e] * dec : 0.f;
+        for (int e = 0; e < 8; ++e) {
+          const int j = chh * 32 + j8 * 8 + e;
+          l[e] = j < i ? nb * __uint_as_float(v[j8 * 8 + e]) * exp2f(g2i - G2[j]) : 0.f;
         }
-        sm.L[i][j0] = l2[0];
-        sm.L[i][j0 + 1] = l2[1];
-        *reinterpret_cast<uint32_t*>(wsA + i * DR_C + j0) = pack_bf16x2(a2[0], a2[1]);
+        *reinterpret_cast<float4*>(dst + j8 * 8) = make_float4(l[0], l[1], l[2], l[3]);
+        *reinterpret_cast<float4*>(dst + j8 * 8 + 4) = make_float4(l[4], l[5], l[6], l[7]);
       }
+    } else {
+      uint4* dst = reinterpret_cast<uint4*>(tile + OFF_A + (size_t)i * 128 + chh * 64);
+#pragma unroll
+      for (int j8 = 0; j8 < 4; ++j8) {
+        float a[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int j = chh * 32 + j8 * 8 + e;
+          a[e] = j <= i ? __uint_as_float(v[j8 * 8 + e]) * exp2f(g2i - G2[j]) : 0.f;
+        }
+        dst[j8] = pack8(a);
+      }
+    }
   }
+  tc_fence_before();
   __syncthreads();
 
-  // 4a. diagonal 16x16 blocks of T = (I - L)^-1: thread (b, c) solves column c of block b,
-  //     keeping the column in registers (no cross-thread dependency).
-  if (tid < 64) {
+  // 5. T = (I - L)^-1 in fp32.  5a: diagonal 16x16 blocks, thread (b, c) solves column c of block b
+  //    with the column in registers.
+  if (ok && tid < 64) {
     const int b0 = (tid >> 4) * 16, c = tid & 15;
     float col[16];
 #pragma unroll
@@ -265,113 +320,125 @@ __global__ void __launch_bounds__(PREP_THREADS, 2) delta_prep_kernel(
       float acc = 0.f;
       if (r == c) acc = 1.f;
       if (r > c) {
-        acc = sm.L[b0 + r][b0 + c];
+        acc = Lf[(b0 + r) * LDF + b0 + c];
 #pragma unroll
         for (int kx = 0; kx < r; ++kx)
-          if (kx > c) acc = fmaf(sm.L[b0 + r][b0 + kx], col[kx], acc);
+          if (kx > c) acc = fmaf(Lf[(b0 + r) * LDF + b0 + kx], col[kx], acc);
       }
       col[r] = acc;
     }
 #pragma unroll
-    for (int r = 0; r < 16; ++r) sm.T[b0 + r][b0 + c] = col[r];
+    for (int r = 0; r < 16; ++r) Tf[(b0 + r) * LDF + b0 + c] = col[r];
   }
   __syncthreads();
-  // 4b. block rows 1..3: T_ij = T_ii * sum_{k=j}^{i-1} L_ik T_kj (M staged in L's upper triangle)
+  // 5b. block rows 1..3: T_ij = T_ii * sum_{k=j}^{i-1} L_ik T_kj (M staged in L's upper triangle)
   for (int bi = 1; bi < 4; ++bi) {
-    for (int e = tid; e < bi * 256; e += PREP_THREADS) {
-      const int bj = e >> 8, rr = (e >> 4) & 15, cc = e & 15;
-      float m = 0.f;
-      for (int x = bj * 16; x < bi * 16; ++x) m = fmaf(sm.L[bi * 16 + rr][x], sm.T[x][bj * 16 + cc], m);
-      sm.L[bj * 16 + rr][bi * 16 + cc] = m;
+    if (ok) {
+      for (int e = tid; e < bi * 256; e += THREADS) {
+        const int bj = e >> 8, rr = (e >> 4) & 15, cc = e & 15;
+        float m = 0.f;
+        for (int x = bj * 16; x < bi * 16; ++x) m = fmaf(Lf[(bi * 16 + rr) * LDF + x], Tf[x * LDF + bj * 16 + cc], m);
+        Lf[(bj * 16 + rr) * LDF + bi * 16 + cc] = m;
+      }
     }
     __syncthreads();
-    for (int e = tid; e < bi * 256; e += PREP_THREADS) {
-      const int bj = e >> 8, rr = (e >> 4) & 15, cc = e & 15;
-      float t = 0.f;
-      for (int x = 0; x <= rr; ++x) t = fmaf(sm.T[bi * 16 + rr][bi * 16 + x], sm.L[bj * 16 + x][bi * 16 + cc], t);
-      sm.T[bi * 16 + rr][bj * 16 + cc] = t;
+    if (ok) {
+      for (int e = tid; e < bi * 256; e += THREADS) {
+        const int bj = e >> 8, rr = (e >> 4) & 15, cc = e & 15;
+        float t = 0.f;
+        for (int x = 0; x <= rr; ++x) t = fmaf(Tf[(bi * 16 + rr) * LDF + bi * 16 + x], Lf[(bj * 16 + x) * LDF + bi * 16 + cc], t);
+        Tf[(bi * 16 + rr) * LDF + bj * 16 + cc] = t;
+      }
     }
     __syncthreads();
   }
 
-  // 5. TU = bf16(T diag(beta)), TW = bf16(T diag(beta e^G)) into q's space (upper triangle = 0)
-  __nv_bfloat16* TU = sm.q;
-  __nv_bfloat16* TW = sm.q + DR_C * DR_C;
-  for (int e = tid; e < DR_C * 8; e += PREP_THREADS) {
-    const int r = e & 63, c0 = (e >> 6) << 3;
-    float t8[8], tu[8], tw[8];
-    *reinterpret_cast<float4*>(&t8[0]) = *reinterpret_cast<const float4*>(&sm.T[r][c0]);
-    *reinterpret_cast<float4*>(&t8[4]) = *reinterpret_cast<const float4*>(&sm.T[r][c0 + 4]);
-    const bool live = (c0 >> 4) <= (r >> 4);
+  // 6. TU = bf16(T diag(beta)), TW = bf16(T diag(beta e^G)) as K-major swizzled B tiles (over L)
+  if (ok) {
+    for (int e = tid; e < 64 * 8; e += THREADS) {
+      const int r = e & 63, c8 = e >> 6;
+      float t8[8], tu[8], tw[8];
+      *reinterpret_cast<float4*>(&t8[0]) = *reinterpret_cast<const float4*>(Tf + r * LDF + c8 * 8);
+      *reinterpret_cast<float4*>(&t8[4]) = *reinterpret_cast<const float4*>(Tf + r * LDF + c8 * 8 + 4);
+      const bool live = (c8 >> 1) <= (r >> 4);  // block-lower part of T (its upper blocks are unset)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float t = live ? t8[j] : 0.f;
+        tu[j] = t * bet[c8 * 8 + j];
+        tw[j] = t * fw[c8 * 8 + j];
+      }
+      const uint32_t off = (uint32_t)r * 128u + ((uint32_t)(c8 ^ (r & 7)) << 4);
+      *reinterpret_cast<uint4*>(sb + TU_OFF + off) = pack8(tu);
+      *reinterpret_cast<uint4*>(sb + TW_OFF + off) = pack8(tw);
+    }
+    fence_proxy_async_smem();
+  }
+  tc_fence_before();
+  __syncthreads();
+
+  // 7. U^T = V^T TU^T and W^T = K^T TW^T  (M128 N64 K64; A = V / K^ MN-major, B = TU / TW K-major)
+  if (ok && tid == 0) {
+    if (mbar_wait(bar0 + 8 * B_V, 0, abort_flag)) {
+      tc_fence_after();
+      constexpr uint32_t ID = idesc_bf16(128, 64, true, false);
+#pragma unroll
+      for (int kt = 0; kt < 4; ++kt) {
+        umma_ss(tmem + TM_U, sdesc_sw128(base + A1 + 8192 + kt * 2048, 16384, 1024),
+                sdesc_sw128(base + TU_OFF + kt * 32, 16, 1024), ID, kt > 0 ? 1u : 0u);
+        umma_ss(tmem + TM_W, sdesc_sw128(base + A1 + kt * 2048, 16384, 1024),
+                sdesc_sw128(base + TW_OFF + kt * 32, 16, 1024), ID, kt > 0 ? 1u : 0u);
+      }
+      umma_commit(bar0 + 8 * B_MMA2);
+    }
+  }
+  if (ok) ok = warp_wait(bar0 + 8 * B_MMA2, 0, abort_flag);
+  // 8. U^T rows (warps 0-3) and W^T rows (warps 4-7) -> workspace, one 128-byte row per thread
+  if (ok) {
+    tc_fence_after();
+    const int q4 = warp & 3, which = warp >> 2;
+    const int r = q4 * 32 + lane;
+    uint32_t v[2][32];
+    const uint32_t ta = tmem + ((uint32_t)(q4 * 32) << 16) + (which ? TM_W : TM_U);
+    tmem_ld32(ta, v[0]);
+    tmem_ld32(ta + 32, v[1]);
+    tmem_ld_wait();
+    uint4* dst = reinterpret_cast<uint4*>(tile + (which ? OFF_W : OFF_UT) + (size_t)r * 128);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const int c = c0 + j;
-      const float t = live ? t8[j] : 0.f;
-      tu[j] = t * sm.beta[c];
-      tw[j] = t * sm.beta[c] * expf(sm.G[c]);
+      float f[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[j >> 2][(j & 3) * 8 + e]);
+      dst[j] = pack8(f);
     }
-    *reinterpret_cast<uint4*>(&TU[swz<DR_C>(r, c0)]) = pack8(tu);
-    *reinterpret_cast<uint4*>(&TW[swz<DR_C>(r, c0)]) = pack8(tw);
   }
+  // teardown: on a bounded-wait failure, let in-flight copies and MMAs land before TMEM and
+  // shared memory are released
+  if (tid == 0 && *abort_flag) {
+    volatile int never = 0;
+    mbar_wait(bar0 + 8 * B_QK, 0, &never, DRAIN_BUDGET);
+    if (issued_v) mbar_wait(bar0 + 8 * B_V, 0, &never, DRAIN_BUDGET);
+    if (issued_mma) {  // every MMA this thread issued has completed
+      umma_commit(bar0 + 8 * B_DRAIN);
+      mbar_wait(bar0 + 8 * B_DRAIN, 0, &never, DRAIN_BUDGET);
+    }
+    atomicExch(&g_delta_error, 1);
+  }
+  tc_fence_before();
   __syncthreads();
-
-  // 6. U = TU V and W = TW K: warp w -> rows [16 (w%4), +16), cols [64 (w/4), +64)
-  {
-    const int r0 = (warp & 3) * 16, n0 = (warp >> 2) * 64;
-    float u[8][4], w[8][4];
-#pragma unroll
-    for (int n = 0; n < 8; ++n)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) u[n][j] = w[n][j] = 0.f;
-#pragma unroll
-    for (int ks = 0; ks < DR_C; ks += 16) {
-      uint32_t au[4], aw[4];
-      lda_sw<DR_C>(TU, r0, ks, au);
-      lda_sw<DR_C>(TW, r0, ks, aw);
-#pragma unroll
-      for (int n = 0; n < 8; n += 2) {
-        uint32_t bv[4], bk[4];
-        ldb_kn_sw<DR_D>(sm.v, n0 + n * 8, ks, bv);
-        ldb_kn_sw<DR_D>(sm.k, n0 + n * 8, ks, bk);
-        mma_bf16_16816(u[n], au, bv[0], bv[1]);
-        mma_bf16_16816(u[n + 1], au, bv[2], bv[3]);
-        mma_bf16_16816(w[n], aw, bk[0], bk[1]);
-        mma_bf16_16816(w[n + 1], aw, bk[2], bk[3]);
-      }
-    }
-    __syncthreads();  // every warp is done with TU/TW, k and v: stage W and U^T there
-    __nv_bfloat16* Wst = sm.q;   // [64][128] swizzled (conflict-free fragment stores)
-    __nv_bfloat16* Ust = sm.k;   // [128][UT_LD] transposed, padded (spans k and v)
-#pragma unroll
-    for (int n = 0; n < 8; ++n)
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int i = r0 + gq + hh * 8;
-        const int j = n0 + n * 8 + 2 * tq;
-        *reinterpret_cast<uint32_t*>(&Wst[swz<DR_D>(i, j)]) = pack_bf16x2(w[n][hh * 2], w[n][hh * 2 + 1]);
-        Ust[j * UT_LD + i] = __float2bfloat16_rn(u[n][hh * 2]);
-        Ust[(j + 1) * UT_LD + i] = __float2bfloat16_rn(u[n][hh * 2 + 1]);
-      }
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TM_COLS);
   }
-  __syncthreads();
-  {
-    uint4* gW = reinterpret_cast<uint4*>(tile + OFF_W);
-    __nv_bfloat16* gU = reinterpret_cast<__nv_bfloat16*>(tile + OFF_UT);
-    for (int e = tid; e < (int)(TILE128 / 16); e += PREP_THREADS) {
-      gW[e] = *reinterpret_cast<const uint4*>(&sm.q[swz<DR_D>(e >> 4, (e & 15) << 3)]);
-      const int j = e >> 3, c = (e & 7) << 3;
-      *reinterpret_cast<uint4*>(gU + j * DR_C + c) = *reinterpret_cast<const uint4*>(sm.k + j * UT_LD + c);
-    }
-  }
-  if (tid == 0) *reinterpret_cast<float*>(tile + OFF_GAMMA) = expf(sm.G[DR_C - 1]);
 }
+
+}  // namespace dprep
 
 // ------------------------------------------------------------------------------------- recurrence
 // tcgen05 recurrence, persistent: each CTA takes (segment, head) chains from an atomic work counter
 // and runs them chunk by chunk; the tile ring runs ahead across chain boundaries.
 //   TMEM (512 columns of fp32; lane = dv row): S^T [0,128), vn [128,192), o^T [192,256) and
 //   [256,320) (double-buffered so the output epilogue leaves the critical path).
-//   Per chunk n (tiles W, Qg, Kg, Aqk, U^T of the chunk in a 2-stage TMA ring, 128-byte swizzle):
+//   Per chunk n (tiles W^T, Qg, Kg, Aqk, U^T of the chunk in a 2-stage TMA ring, 128-byte swizzle):
 //     state warps : S^T -> bf16 A tile in SMEM; S^T *= gamma in TMEM
 //     MMA thread  : vn = S^T W^T (M128 N64 K128); then o^T = S^T Qg^T
 //     state warps : v_new^T = U^T - vn -> bf16 A tile in SMEM; then o^T of chunk n-1 -> out
@@ -397,8 +464,6 @@ constexpr int THREADS = 192;
 constexpr uint32_t TM_S = 0, TM_VN = 128, TM_O = 192, TM_COLS = 512;
 constexpr long long DRAIN_BUDGET = 2000000000LL;
 
-__device__ int g_recur_error = 0;
-
 struct RParams {
   const int32_t* cu;
   const int32_t* table;
@@ -415,17 +480,6 @@ struct StageMeta {  // written by the producer before the stage's expect_tx arri
   float gamma;
   int pad[3];
 };
-
-// byte offset of 16-byte chunk `c16` of row `r` in a [c16 / 8][rows][128 B] 128-byte-swizzled tile
-__device__ __forceinline__ uint32_t sw128_off(int r, int c16, int rows) {
-  return (uint32_t)(c16 >> 3) * (uint32_t)(rows * 128) + (uint32_t)r * 128u + ((uint32_t)((c16 & 7) ^ (r & 7)) << 4);
-}
-
-// warp-uniform bounded wait: every lane polls, the warp proceeds only if all lanes saw the phase
-__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
-  const bool ok = mbar_wait(bar, parity, abort_flag);
-  return __all_sync(0xffffffffu, ok ? 1 : 0) != 0;
-}
 
 __global__ void __launch_bounds__(THREADS, 1)
 delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_constant__ CUtensorMap mqg,
@@ -493,7 +547,6 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
           const uint32_t fb = bar0 + 8 * (B_FULL0 + st);
           mbar_expect_tx(fb, ST_BYTES);
           tma_load_3d(sb + ST_W, &mw, fb, 0, 0, z);
-          tma_load_3d(sb + ST_W + KM_HALF, &mw, fb, 64, 0, z);
           tma_load_3d(sb + ST_QG, &mqg, fb, 0, 0, z);
           tma_load_3d(sb + ST_QG + KM_HALF, &mqg, fb, 64, 0, z);
           tma_load_3d(sb + ST_KG, &mkg, fb, 0, 0, z);
@@ -515,6 +568,7 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t ID_N64 = idesc_bf16(128, 64, false, false);
+      constexpr uint32_t ID_N64_BMN = idesc_bf16(128, 64, false, true);
       constexpr uint32_t ID_N128_BMN = idesc_bf16(128, 128, false, true);
       for (int n = 0;; ++n) {
         const int st = n & 1;
@@ -524,13 +578,12 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
         if (!mbar_wait(bar0 + 8 * B_SA, n & 1, abort_flag)) break;
         tc_fence_after();
         const uint32_t tO = tmem + TM_O + 64u * (uint32_t)st;
-        // vn = S^T W^T  (K = 128 dk: 2 swizzle halves x 4 steps of 16)
+        // vn = S^T W^T  (K = 128 dk: 2 swizzle halves x 4 steps of 16; W^T [dk][tok] is MN-major)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t aoff = (uint32_t)(kk >> 2) * (128u * 128u) + (uint32_t)(kk & 3) * 32u;
-          const uint32_t boff = (uint32_t)(kk >> 2) * KM_HALF + (uint32_t)(kk & 3) * 32u;
-          umma_ss(tmem + TM_VN, sdesc_sw128(base + OFF_SA + aoff, 16, 1024), sdesc_sw128(sb + ST_W + boff, 16, 1024),
-                  ID_N64, kk > 0 ? 1u : 0u);
+          umma_ss(tmem + TM_VN, sdesc_sw128(base + OFF_SA + aoff, 16, 1024),
+                  sdesc_sw128(sb + ST_W + (uint32_t)kk * 2048u, KM_HALF, 1024), ID_N64_BMN, kk > 0 ? 1u : 0u);
         }
         umma_commit(bar0 + 8 * B_VN);
         // o^T = S^T Qg^T
@@ -695,7 +748,7 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
     tc_fence_after();
     tmem_dealloc(tmem, TM_COLS);
   }
-  if (tid == 0 && *abort_flag) atomicExch(&g_recur_error, 1);
+  if (tid == 0 && *abort_flag) atomicExch(&g_delta_error, 1);
 }
 
 // Final state of empty segments (their chains never enter the recurrence): the initial state, or 0.
@@ -742,17 +795,34 @@ static int tile_map(CUtensorMap* m, const uint8_t* tiles, size_t off, int cols, 
   return FDK_OK;
 }
 
+// 2-D map over a [tokens, >= heads * 128] bf16 activation (row stride ld elements), box 64 x 64,
+// 128-byte swizzle: one (chunk, head) tile is two boxes.
+static int act_map(CUtensorMap* m, const void* ptr, int64_t tokens, int64_t heads, int64_t ld) {
+  EncodeFn enc = encode_fn();
+  if (!enc) return set_error(FDK_ERR_DEVICE, "chunk_gated_delta_rule: cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)(heads * DR_D), (cuuint64_t)tokens};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {64, 64};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(FDK_ERR_INVALID_ARGUMENT, "chunk_gated_delta_rule: tensor map encode failed (%d)", (int)r);
+  return FDK_OK;
+}
+
 }  // namespace drtc
 
 int delta_take_device_error() {
   int h = 0;
-  if (cudaMemcpyFromSymbol(&h, drtc::g_recur_error, sizeof(int)) != cudaSuccess) {
+  if (cudaMemcpyFromSymbol(&h, g_delta_error, sizeof(int)) != cudaSuccess) {
     cudaGetLastError();
     return -1;
   }
   if (h) {
     int zero = 0;
-    cudaMemcpyToSymbol(drtc::g_recur_error, &zero, sizeof(int));
+    cudaMemcpyToSymbol(g_delta_error, &zero, sizeof(int));
   }
   return h;
 }
@@ -765,7 +835,7 @@ static int launch_recur(int nseg, int heads, int64_t n_tiles, cudaStream_t s, co
     if (int st = check_launch("chunk_gated_delta_rule/empty segments")) return st;
   }
   CUtensorMap mw, mqg, mkg, ma, mut;
-  if (int st = tile_map(&mw, tiles, OFF_W, DR_D, DR_C, n_tiles)) return st;
+  if (int st = tile_map(&mw, tiles, OFF_W, DR_C, DR_D, n_tiles)) return st;
   if (int st = tile_map(&mqg, tiles, OFF_QG, DR_D, DR_C, n_tiles)) return st;
   if (int st = tile_map(&mkg, tiles, OFF_KG, DR_D, DR_C, n_tiles)) return st;
   if (int st = tile_map(&ma, tiles, OFF_A, DR_C, DR_C, n_tiles)) return st;
@@ -817,23 +887,26 @@ extern "C" int fdk_chunk_gated_delta_rule_fwd(const void* q, const void* k, int6
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   int32_t* table = reinterpret_cast<int32_t*>(ws + lay.off_table);
+  int2* info = reinterpret_cast<int2*>(ws + lay.off_info);
   uint8_t* tiles = ws + lay.off_tiles;
   const int nseg = (int)num_segments;
-  chunk_table_kernel<<<1, 32, 0, s>>>(cu_seqlens, nseg, table);
+  chunk_table_kernel<<<1, 256, 0, s>>>(cu_seqlens, nseg, table, info);
   if (int st = check_launch("chunk_gated_delta_rule/table")) return st;
   if (tokens == 0 && !final_state) return FDK_OK;
-  static bool attr_set[64] = {};
-  const int prep_smem = (int)sizeof(PrepSmem);
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaFuncSetAttribute(delta_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem);
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
-  }
   if (tokens > 0) {
-    delta_prep_kernel<<<dim3((unsigned)lay.max_chunks, (unsigned)heads), PREP_THREADS, prep_smem, s>>>(
-        static_cast<const bf16*>(q), static_cast<const bf16*>(k), ld_qk, static_cast<const bf16*>(v), ld_v, g,
-        static_cast<const bf16*>(beta), cu_seqlens, nseg, table, (int)heads, scale, tiles);
+    CUtensorMap mq, mk, mv;
+    if (int st = drtc::act_map(&mq, q, tokens, heads, ld_qk)) return st;
+    if (int st = drtc::act_map(&mk, k, tokens, heads, ld_qk)) return st;
+    if (int st = drtc::act_map(&mv, v, tokens, heads, ld_v)) return st;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+      cudaFuncSetAttribute(dprep::delta_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dprep::SMEM_BYTES);
+      if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+    dprep::delta_prep_kernel<<<dim3((unsigned)lay.max_chunks, (unsigned)heads), dprep::THREADS, dprep::SMEM_BYTES, s>>>(
+        mq, mk, mv, g, static_cast<const bf16*>(beta), info, table, nseg, (int)heads, scale, tiles);
     if (int st = check_launch("chunk_gated_delta_rule/prep")) return st;
   }
   return launch_recur(nseg, (int)heads, lay.max_chunks * heads, s, cu_seqlens, table, table + nseg + 1, tiles,
