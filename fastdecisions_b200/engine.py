@@ -133,18 +133,24 @@ class DecisionEngine:
                 L.k_norm = put(w[sa + "k_norm.weight"])
                 L.w_o = put(w[sa + "o_proj.weight"])
             self.layers.append(L)
-        self._ws: Optional[torch.Tensor] = None
+        self._ws: dict = {}
         self._graphs = {}
-        self._pinned: Optional[torch.Tensor] = None
+        self._pinned_slots: list = []   # per stream: [pinned int32 host buffer, event after its H2D]
+        self._streams: list = []
         self.stats = dict(forwards=0, graph_captures=0, graph_replays=0)
         self.kernel_timer = None  # optional callable(name) -> context manager, set by the bench
 
     # ------------------------------------------------------------------ workspace
     def _workspace(self, tokens: int, segments: int) -> torch.Tensor:
+        """Delta-rule scratch of the current stream (one buffer per stream, so batches in flight on
+        different streams never share it)."""
         need = ops.delta_rule_workspace_bytes(tokens, segments, self.cfg.linear_num_value_heads)
-        if self._ws is None or self._ws.numel() < need:
-            self._ws = torch.empty(need, device=self.dev, dtype=torch.uint8)
-        return self._ws
+        key = torch.cuda.current_stream(self.dev).cuda_stream
+        ws = self._ws.get(key)
+        if ws is None or ws.numel() < need:
+            ws = torch.empty(need, device=self.dev, dtype=torch.uint8)
+            self._ws[key] = ws
+        return ws
 
     def reserve(self, tokens: int, segments: int):
         """Pre-size the delta-rule scratch (call before graph capture)."""
@@ -265,16 +271,70 @@ class DecisionEngine:
             off += p.size
         return out, n * 4
 
+    def streams(self, n: int) -> list:
+        """``n`` CUDA streams of this engine (created once); batches are spread over them."""
+        while len(self._streams) < n:
+            self._streams.append(torch.cuda.Stream(self.dev))
+        return self._streams[:n]
+
     @torch.no_grad()
-    def score(self, requests: Sequence[Request]) -> np.ndarray:
-        """Public API: decision probabilities ``[N, K]`` (numpy) for host-side requests."""
-        batch = pack(requests)
-        n = batch.tokens * 2 + 3 * batch.num_segments + 1
-        if self._pinned is None or self._pinned.numel() < n:
-            self._pinned = torch.empty(max(n, 1 << 16), dtype=torch.int32, pin_memory=True)
-        (ids, cu, pos, slots, nopts), _ = self.to_device(batch, self._pinned)
-        probs, _ = self.forward_device(ids, cu, pos, slots, nopts, batch.max_seqlen)
-        return probs.cpu().numpy()
+    def forward_batches(self, dev_batches: Sequence, max_seqlens: Sequence[int], probs: Sequence[torch.Tensor],
+                        streams: int = 2):
+        """Forward of several packed device batches, batch ``k`` on stream ``k % streams``: kernels
+        of one batch fill the SMs another batch leaves idle (the delta-rule recurrence runs one chain
+        per SM; short kernels have tails).  ``probs[k]`` receives batch ``k``'s answer rows.  The
+        current stream waits for all of them on return."""
+        main = torch.cuda.current_stream(self.dev)
+        sts = self.streams(max(1, streams))
+        for st in sts:
+            st.wait_stream(main)
+        for k, ((ids, cu, pos, slots, nopts), ms, pr) in enumerate(zip(dev_batches, max_seqlens, probs)):
+            with torch.cuda.stream(sts[k % len(sts)]):
+                self.forward_device(ids, cu, pos, slots, nopts, ms, probs=pr)
+        for st in sts:
+            main.wait_stream(st)
+
+    @torch.no_grad()
+    def score(self, requests: Sequence[Request], max_tokens: int = 32768, streams: int = 2) -> np.ndarray:
+        """Public API: decision probabilities ``[N, K]`` (numpy, request order) for host-side requests.
+
+        Requests are packed longest-first into batches of at most ``max_tokens`` tokens
+        (``plan_batches``); each batch is packed on the host while the previous ones run, copied in
+        one pinned H2D transfer, run on stream ``k % streams``, and its answer rows come back in one
+        D2H copy into pinned host memory."""
+        if len(requests) == 0:
+            return np.zeros((0, self.letters.shape[0]), dtype=np.float32)
+        plan = plan_batches([r.ids.size for r in requests], max_tokens)
+        K = self.letters.shape[0]
+        sts = self.streams(max(1, streams))
+        main = torch.cuda.current_stream(self.dev)
+        for st in sts:
+            st.wait_stream(main)
+        host_out = torch.empty((len(requests), K), dtype=torch.float32, pin_memory=True)
+        while len(self._pinned_slots) < len(sts):
+            self._pinned_slots.append([None, torch.cuda.Event()])
+        row = 0
+        for k, b in enumerate(plan):
+            batch = pack([requests[j] for j in b])  # host work overlaps the batches already queued
+            slot = self._pinned_slots[k % len(sts)]
+            n = batch.tokens * 2 + 3 * batch.num_segments + 1
+            slot[1].synchronize()  # the previous H2D from this pinned buffer has finished
+            if slot[0] is None or slot[0].numel() < n:
+                slot[0] = torch.empty(max(n, 1 << 16), dtype=torch.int32, pin_memory=True)
+            st = sts[k % len(sts)]
+            with torch.cuda.stream(st):
+                (ids, cu, pos, slots, nopts), _ = self.to_device(batch, slot[0])
+                slot[1].record(st)
+                probs, _ = self.forward_device(ids, cu, pos, slots, nopts, batch.max_seqlen)
+                host_out[row:row + len(b)].copy_(probs, non_blocking=True)
+            row += len(b)
+        for st in sts:
+            main.wait_stream(st)
+        main.synchronize()
+        order = np.concatenate([np.asarray(b, dtype=np.int64) for b in plan])
+        result = np.empty((len(requests), K), dtype=np.float32)
+        result[order] = host_out.numpy()
+        return result
 
     # ------------------------------------------------------------------ CUDA graphs
     @torch.no_grad()
