@@ -7,9 +7,10 @@
 //   warp  8    TMA producer: Q (once), K ring of 2 stages, V single stage
 //   warp  9    TMEM allocator + single-thread tcgen05.mma issuer
 // TMEM (512 columns): S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512), fp32.
-// Per KV block j the issuer runs S_A = Q_A K_j^T, S_B = Q_B K_j^T, then O_A += P_A V_j once the
-// head-A softmax has written P_A (bf16, 128B-swizzled K-major tile in shared memory), then
-// O_B += P_B V_j.  While one head's softmax runs, the tensor core works on the other head.
+// The issuer runs S_A = Q_A K_0^T and S_B = Q_B K_0^T, then per KV block j: O_A += P_A V_j once
+// the head-A softmax has written P_A (bf16, 128B-swizzled K-major tile in shared memory),
+// S_A = Q_A K_{j+1}^T, O_B += P_B V_j, S_B = Q_B K_{j+1}^T.  Head A's softmax of block j+1 thus
+// overlaps head B's of block j, and the tensor core always has the other head's work queued.
 // Softmax is online in fp32 in the exp2 domain with lazy rescaling of O (only when the running
 // max grows by more than 2^8).  The causal mask is applied only on the diagonal block; rows of a
 // tile past the end of its segment are computed but never stored.  Varlen: cu_seqlens gives
@@ -129,44 +130,53 @@ gqa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     if (lane == 0) {
       constexpr uint32_t ID_QK = idesc_bf16(128, 128, false, false);
       constexpr uint32_t ID_PV = idesc_bf16(128, 128, false, true);  // V is MN-major (D contiguous)
-      bool ok = mbar_wait(bar0 + 8 * B_Q, 0, abort_flag);
-      tc_fence_after();
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int ks = j & 1;
-        if (!mbar_wait(bar0 + 8 * (B_KF0 + ks), (j >> 1) & 1, abort_flag)) break;
+      // Issue order per KV block j: PV_A(j), S_A(j+1), PV_B(j), S_B(j+1).  Softmax A starts on
+      // block j+1 while softmax B is still on block j, so the two row groups overlap each other
+      // and the tensor pipe instead of taking turns.  Each S commit also covers the PV of the
+      // same head issued before it (O rescale and P-tile reuse rely on that).
+      auto issue_s = [&](int j, uint32_t q_off, uint32_t tm, uint32_t bar) {
+        const uint32_t kb = base + ((j & 1) ? OFF_K1 : OFF_K0);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
+          umma_ss(tmem + tm, sdesc_sw128(base + q_off + off, 16, 1024), sdesc_sw128(kb + off, 16, 1024), ID_QK, kk > 0);
+        }
+        umma_commit(bar);
+      };
+      auto issue_pv = [&](int j, uint32_t p_off, uint32_t tm) {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t aoff = (kk >> 2) * HALF + (kk & 3) * 32;
+          umma_ss(tmem + tm, sdesc_sw128(base + p_off + aoff, 16, 1024),
+                  sdesc_sw128(base + OFF_V + kk * 2048, HALF, 1024), ID_PV, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(bar0 + 8 * B_Q, 0, abort_flag) && mbar_wait(bar0 + 8 * B_KF0, 0, abort_flag);
+      if (ok) {
         tc_fence_after();
-        const uint32_t kb = base + (ks ? OFF_K1 : OFF_K0);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
-          umma_ss(tmem + TM_SA, sdesc_sw128(base + OFF_QA + off, 16, 1024), sdesc_sw128(kb + off, 16, 1024), ID_QK, kk > 0);
-        }
-        umma_commit(bar0 + 8 * B_SA);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
-          umma_ss(tmem + TM_SB, sdesc_sw128(base + OFF_QB + off, 16, 1024), sdesc_sw128(kb + off, 16, 1024), ID_QK, kk > 0);
-        }
-        umma_commit(bar0 + 8 * B_SB);
-        umma_commit(bar0 + 8 * (B_KE0 + ks));
+        issue_s(0, OFF_QA, TM_SA, bar0 + 8 * B_SA);
+        issue_s(0, OFF_QB, TM_SB, bar0 + 8 * B_SB);
+        umma_commit(bar0 + 8 * B_KE0);
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const bool more = j + 1 < n_kv;
         if (!mbar_wait(bar0 + 8 * B_VF, j & 1, abort_flag)) break;
         if (!mbar_wait(bar0 + 8 * B_PA, j & 1, abort_flag)) break;
         tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t aoff = (kk >> 2) * HALF + (kk & 3) * 32;
-          umma_ss(tmem + TM_OA, sdesc_sw128(base + OFF_PA + aoff, 16, 1024),
-                  sdesc_sw128(base + OFF_V + kk * 2048, HALF, 1024), ID_PV, (j > 0 || kk > 0) ? 1u : 0u);
+        issue_pv(j, OFF_PA, TM_OA);
+        if (more) {
+          if (!mbar_wait(bar0 + 8 * (B_KF0 + ((j + 1) & 1)), ((j + 1) >> 1) & 1, abort_flag)) break;
+          tc_fence_after();
+          issue_s(j + 1, OFF_QA, TM_SA, bar0 + 8 * B_SA);
         }
         if (!mbar_wait(bar0 + 8 * B_PB, j & 1, abort_flag)) break;
         tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t aoff = (kk >> 2) * HALF + (kk & 3) * 32;
-          umma_ss(tmem + TM_OB, sdesc_sw128(base + OFF_PB + aoff, 16, 1024),
-                  sdesc_sw128(base + OFF_V + kk * 2048, HALF, 1024), ID_PV, (j > 0 || kk > 0) ? 1u : 0u);
-        }
+        issue_pv(j, OFF_PB, TM_OB);
         umma_commit(bar0 + 8 * B_VE);
+        if (more) {
+          issue_s(j + 1, OFF_QB, TM_SB, bar0 + 8 * B_SB);
+          umma_commit(bar0 + 8 * (B_KE0 + ((j + 1) & 1)));
+        }
       }
       umma_commit(bar0 + 8 * B_O);  // arrives when every MMA above has completed
       drain(bar0 + 8 * B_O, 0);
