@@ -71,12 +71,17 @@ gqa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_BAR + 8 * NBAR + 4);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int seg0 = p.cu[blockIdx.y];
-  const int L = p.cu[blockIdx.y + 1] - seg0;
-  const int mblk = (int)gridDim.x - 1 - (int)blockIdx.x;  // longest tiles first
+  // grid: x = (segment, head pair) with the pair fastest, y = query tile from the last one down.
+  // Blocks are dispatched x-fastest, so every segment's longest (causal: most KV blocks) tiles go
+  // first across all heads -- longest-processing-time order over the whole grid.
+  const int npairs = p.hq / 2;
+  const int seg = (int)blockIdx.x / npairs, pair = (int)blockIdx.x - seg * npairs;
+  const int seg0 = p.cu[seg];
+  const int L = p.cu[seg + 1] - seg0;
+  const int mblk = (int)gridDim.y - 1 - (int)blockIdx.y;
   const int m0 = mblk * BM;
   if (m0 >= L) return;  // uniform early exit: this tile lies past the segment
-  const int ha = blockIdx.z * 2, hb = ha + 1;
+  const int ha = pair * 2, hb = ha + 1;
   const int hk = ha / (p.hq / p.hkv);
   const int n_kv = mblk + 1;
 
@@ -202,17 +207,23 @@ gqa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, sr[c]);
       tmem_ld_wait();
-      const bool diag = (j == n_kv - 1);
-      float mx = -INFINITY;
+      if (j == n_kv - 1) {  // diagonal block: causal mask (the only block that needs one)
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (c * 32 + i > row) sr[c][i] = __float_as_uint(-INFINITY);
+      }
+      // row max with 8 independent accumulators (a 128-long fmax chain would serialise the warp)
+      float mx8[8];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) mx8[a] = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float v = __uint_as_float(sr[c][i]);
-          if (diag && (c * 32 + i) > row) v = -INFINITY;
-          sr[c][i] = __float_as_uint(v);
-          mx = fmaxf(mx, v);
-        }
+        for (int i = 0; i < 32; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sr[c][i]));
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float m_new = fmaxf(m_run, mx * sl2);
       float alpha = 1.f;
       bool rescale = false;
@@ -223,8 +234,11 @@ gqa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
         m_run = m_new;
         rescale = true;
       }
-      // P = exp2(S * scale * log2e - m_run) as bf16 into the swizzled K-major tile
-      float sum = 0.f;
+      // P = exp2(S * scale * log2e - m_run) as bf16 into the swizzled K-major tile; the row sum
+      // in 8 independent partial sums
+      float sum8[8];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) sum8[a] = 0.f;
 #pragma unroll
       for (int c16 = 0; c16 < 16; ++c16) {
         float e[8];
@@ -232,11 +246,12 @@ gqa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
         for (int i = 0; i < 8; ++i) {
           const int col = c16 * 8 + i;
           e[i] = ex2(fmaf(__uint_as_float(sr[col >> 5][col & 31]), sl2, -m_run));
-          sum += e[i];
+          sum8[i] += e[i];
         }
         const uint32_t off = (uint32_t)(c16 >> 3) * HALF + (uint32_t)row * 128u + ((uint32_t)((c16 & 7) ^ (row & 7)) << 4);
         *reinterpret_cast<uint4*>(P + off) = pack8(e);
       }
+      const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
       l_run = l_run * alpha + sum;
       if (rescale) {  // O row *= alpha (PV of block j-1 has completed: S_j's commit covers it)
 #pragma unroll
@@ -373,7 +388,9 @@ extern "C" int fdk_gqa_fwd(const void* q, int64_t ld_q, const void* k, int64_t l
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   const int64_t mtiles = (max_seqlen + BM - 1) / BM;
-  dim3 grid((unsigned)mtiles, (unsigned)num_segments, (unsigned)(hq / 2));
+  if (mtiles > 65535 || num_segments * (hq / 2) > 0x7fffffff)
+    return set_error(FDK_ERR_UNSUPPORTED, "gqa_fwd: too many query tiles or segments");
+  dim3 grid((unsigned)(num_segments * (hq / 2)), (unsigned)mtiles);
   gqa_fwd_kernel<<<grid, NUM_THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(mq, mk, mv, prm);
   return check_launch("gqa_fwd");
 }

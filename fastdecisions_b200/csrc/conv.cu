@@ -44,11 +44,12 @@ constexpr int CONV_SROWS = CONV_ROWS + CONV_HALO;
 constexpr int CONV_RPT = 8;             // rows per thread
 
 template <int KW>
-__global__ void __launch_bounds__(CONV_THREADS) packed_conv_silu_smem_kernel(
+__global__ void __launch_bounds__(CONV_THREADS, 6) packed_conv_silu_smem_kernel(
     const bf16* __restrict__ x, int64_t ldx, const bf16* __restrict__ w, int64_t ntok, int64_t period,
     const int32_t* __restrict__ cu, int nseg, int channels, int key_dim, bf16* __restrict__ q,
     bf16* __restrict__ k, bf16* __restrict__ v) {
   __shared__ __align__(16) bf16 tile[2][CONV_SROWS][CONV_CB];
+  __shared__ long long seg_info[CONV_ROWS / CONV_RPT][2];  // per row group: segment start, next start
   const int tid = threadIdx.x;
   const int cb0 = blockIdx.x * CONV_CB;
   const int cq = tid & 15, rg = tid >> 4;   // 8 channels, 8 rows
@@ -89,6 +90,18 @@ __global__ void __launch_bounds__(CONV_THREADS) packed_conv_silu_smem_kernel(
   issue(first, 0);
   for (int64_t ti = first; ti < last; ++ti) {
     const int b = (int)((ti - first) & 1);
+    if (tid < CONV_ROWS / CONV_RPT) {  // segment bounds of the 8 row groups, found once per tile
+      const int64_t rg0 = ti * CONV_ROWS + tid * CONV_RPT;
+      if (rg0 < ntok) {
+        if (cu != nullptr) {
+          seg_info[tid][0] = segment_start(cu, nseg, rg0);
+          seg_info[tid][1] = next_start(cu, nseg, rg0);
+        } else {
+          seg_info[tid][0] = (rg0 / period) * period;
+          seg_info[tid][1] = seg_info[tid][0] + period;
+        }
+      }
+    }
     if (ti + 1 < last) {
       issue(ti + 1, b ^ 1);
       asm volatile("cp.async.wait_group 1;\n" ::);
@@ -98,14 +111,8 @@ __global__ void __launch_bounds__(CONV_THREADS) packed_conv_silu_smem_kernel(
     __syncthreads();
     const int64_t r0 = ti * CONV_ROWS + rg * CONV_RPT;   // first output token of this thread
     if (active && r0 < ntok) {  // predicated, never around a barrier: every thread reaches both __syncthreads
-      int64_t seg0, nxt;
-      if (cu != nullptr) {
-        seg0 = segment_start(cu, nseg, r0);
-        nxt = next_start(cu, nseg, r0);
-      } else {
-        seg0 = (r0 / period) * period;
-        nxt = seg0 + period;
-      }
+      const int64_t seg0 = seg_info[rg][0];
+      int64_t nxt = seg_info[rg][1];
       float hist[3][8];
 #pragma unroll
       for (int j = 0; j < 3; ++j) {
@@ -117,10 +124,14 @@ __global__ void __launch_bounds__(CONV_THREADS) packed_conv_silu_smem_kernel(
         }
       }
       bf16* out = dst + r0 * ldd + cc;
+      const bf16* srow = &tile[b][rg * CONV_RPT + CONV_HALO][cq * 8];
+      // the 8 rows lie inside one segment and inside the batch: no per-row checks
+      const bool plain = nxt >= r0 + CONV_RPT && r0 + CONV_RPT <= ntok;
 #pragma unroll
       for (int i = 0; i < CONV_RPT; ++i) {
         const int64_t t = r0 + i;
-        if (t < ntok) {
+        if (!plain) {
+          if (t >= ntok) break;
           if (t == nxt) {
 #pragma unroll
             for (int j = 0; j < 3; ++j)
@@ -128,23 +139,23 @@ __global__ void __launch_bounds__(CONV_THREADS) packed_conv_silu_smem_kernel(
               for (int c = 0; c < 8; ++c) hist[j][c] = 0.f;
             nxt = (cu != nullptr) ? next_start(cu, nseg, t) : nxt + period;
           }
-          float cur[8], y[8];
-          unpack8(*reinterpret_cast<const uint4*>(&tile[b][rg * CONV_RPT + CONV_HALO + i][cq * 8]), cur);
+        }
+        float cur[8], y[8];
+        unpack8(*reinterpret_cast<const uint4*>(srow + i * CONV_CB), cur);
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            float acc = wr[KW - 1][c] * cur[c];
-            if (KW >= 2) acc = fmaf(wr[KW - 2][c], hist[2][c], acc);
-            if (KW >= 3) acc = fmaf(wr[KW - 3][c], hist[1][c], acc);
-            if (KW >= 4) acc = fmaf(wr[KW - 4][c], hist[0][c], acc);
-            y[c] = silu_tanh(acc);
-          }
-          *reinterpret_cast<uint4*>(out + i * ldd) = pack8(y);
+        for (int c = 0; c < 8; ++c) {
+          float acc = wr[KW - 1][c] * cur[c];
+          if (KW >= 2) acc = fmaf(wr[KW - 2][c], hist[2][c], acc);
+          if (KW >= 3) acc = fmaf(wr[KW - 3][c], hist[1][c], acc);
+          if (KW >= 4) acc = fmaf(wr[KW - 4][c], hist[0][c], acc);
+          y[c] = silu_tanh(acc);
+        }
+        *reinterpret_cast<uint4*>(out + i * ldd) = pack8(y);
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            hist[0][c] = hist[1][c];
-            hist[1][c] = hist[2][c];
-            hist[2][c] = cur[c];
-          }
+        for (int c = 0; c < 8; ++c) {
+          hist[0][c] = hist[1][c];
+          hist[1][c] = hist[2][c];
+          hist[2][c] = cur[c];
         }
       }
     }
@@ -184,6 +195,17 @@ extern "C" int fdk_packed_conv_silu(const void* x, int64_t ld_x, const void* wei
   auto kb = static_cast<bf16*>(k);
   auto vb = static_cast<bf16*>(v);
   const int nseg = (int)num_segments;
+  static bool carveout_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !carveout_set[dev]) {
+    // 34 KB of static shared memory per CTA: ask for the full carveout so six CTAs fit per SM
+    cudaFuncSetAttribute(packed_conv_silu_smem_kernel<4>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaFuncSetAttribute(packed_conv_silu_smem_kernel<3>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaFuncSetAttribute(packed_conv_silu_smem_kernel<2>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaFuncSetAttribute(packed_conv_silu_smem_kernel<1>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (dev >= 0 && dev < 64) carveout_set[dev] = true;
+  }
   switch (kernel_width) {
     case 4: packed_conv_silu_smem_kernel<4><<<grid, CONV_THREADS, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
     case 3: packed_conv_silu_smem_kernel<3><<<grid, CONV_THREADS, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;

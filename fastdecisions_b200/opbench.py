@@ -127,17 +127,20 @@ def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--op", default="all", help="one of %s, or all" % ", ".join(OPS))
     ap.add_argument("--batch", type=int, default=0, help="index into the config-5 batch plan")
+    ap.add_argument("--lens", default=None,
+                    help="comma-separated request lengths to pack instead of a config-5 batch (e.g. 4096)")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     args = ap.parse_args(argv)
     cfg = ModelConfig()
-    lens = batch_lengths(args.batch)
+    lens = [int(x) for x in args.lens.split(",")] if args.lens else batch_lengths(args.batch)
     peaks = _peaks()
     for op in (OPS if args.op == "all" else (args.op,)):
         fn, (bound, work) = make_case(op, lens, cfg)
         ms = time_op(fn, args.iters, args.warmup)
         achieved = work / (ms * 1e-3) / (1e12 if bound == "tensor" else 1e9)
-        print(json.dumps({"op": op, "batch": args.batch, "tokens": int(sum(lens)), "segments": len(lens),
+        print(json.dumps({"op": op, "batch": "lens" if args.lens else args.batch, "tokens": int(sum(lens)),
+                          "segments": len(lens),
                           "max_len": int(max(lens)), "us": round(ms * 1e3, 2), "bound": bound,
                           "achieved": round(achieved, 1), "unit": "TFLOP/s" if bound == "tensor" else "GB/s",
                           "frac": round(achieved / peaks[bound], 4), "peak_source": peaks["source"]}), flush=True)
