@@ -7,9 +7,10 @@
 //   2. delta_prep_kernel  : one 256-thread CTA per (chunk, head), fully parallel, three CTAs per
 //      SM.  TMA brings the raw q / k rows, the CTA l2-normalises them, takes the in-chunk cumsum G
 //      of the log decay, forms [K;Q] K^T as one M=128 tcgen05 MMA, inverts the unit-lower-
-//      triangular (I - L) in fp32 on the CUDA cores (16x16 diagonal blocks by forward
-//      substitution, then block forward substitution), and forms U^T and W^T as two more MMAs
-//      (V and K as MN-major A operands).  It writes into the caller's workspace (bf16)
+//      triangular (I - L) from 16x16 block products (diagonal blocks by repeated squaring, then
+//      block forward substitution; mma.sync tf32 with the 3xTF32 split, fp32-accurate), and
+//      forms U^T and W^T as two more tcgen05 MMAs (V and K as MN-major A operands).  It writes
+//      into the caller's workspace (bf16)
 //        W^T = (T diag(beta e^G) K)^T   U^T = (T diag(beta) V)^T     Aqk = (QK^T o decay), lower
 //        Qg  = q e^G                    Kg  = k e^(G_last - G)       gamma = e^G_last (fp32)
 //   3. delta_recur_tc_kernel : persistent; each CTA takes (segment, head) chains from a work
@@ -109,6 +110,61 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
 }
 
 __device__ int g_delta_error = 0;  // set when a bounded wait of a delta-rule kernel ran out
+
+// ---- 16x16 fp32 block products on the tensor cores: mma.sync m16n8k8 tf32 with the 3xTF32 split
+//      (x = hi + lo, both tf32; x*y ~ hi*hi + hi*lo + lo*hi), accurate to about fp32.  One warp per
+//      product; blocks are row-major in shared memory with row stride ld floats.
+__device__ __forceinline__ void tf32_split(float x, uint32_t& hi, uint32_t& lo) {
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(hi) : "f"(x));
+  const float r = x - __uint_as_float(hi);
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(lo) : "f"(r));
+}
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// acc = C (or 0 when C is null), in the m16n8 accumulator layout of two 8-column tiles
+__device__ __forceinline__ void bmm16_init(float (&acc)[2][4], const float* C, int ld) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    acc[nt][0] = C ? C[g * ld + nt * 8 + 2 * t] : 0.f;
+    acc[nt][1] = C ? C[g * ld + nt * 8 + 2 * t + 1] : 0.f;
+    acc[nt][2] = C ? C[(g + 8) * ld + nt * 8 + 2 * t] : 0.f;
+    acc[nt][3] = C ? C[(g + 8) * ld + nt * 8 + 2 * t + 1] : 0.f;
+  }
+}
+// acc += X Y (16x16 each)
+__device__ __forceinline__ void bmm16_acc(float (&acc)[2][4], const float* X, const float* Y, int ld) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int k0 = 0; k0 < 16; k0 += 8) {
+    uint32_t ah[4], al[4];
+    tf32_split(X[g * ld + k0 + t], ah[0], al[0]);
+    tf32_split(X[(g + 8) * ld + k0 + t], ah[1], al[1]);
+    tf32_split(X[g * ld + k0 + t + 4], ah[2], al[2]);
+    tf32_split(X[(g + 8) * ld + k0 + t + 4], ah[3], al[3]);
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      uint32_t bh0, bl0, bh1, bl1;
+      tf32_split(Y[(k0 + t) * ld + nt * 8 + g], bh0, bl0);
+      tf32_split(Y[(k0 + t + 4) * ld + nt * 8 + g], bh1, bl1);
+      mma_tf32(acc[nt], al, bh0, bh1);
+      mma_tf32(acc[nt], ah, bl0, bl1);
+      mma_tf32(acc[nt], ah, bh0, bh1);
+    }
+  }
+}
+__device__ __forceinline__ void bmm16_store(const float (&acc)[2][4], float* C, int ld) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    *reinterpret_cast<float2*>(C + g * ld + nt * 8 + 2 * t) = make_float2(acc[nt][0], acc[nt][1]);
+    *reinterpret_cast<float2*>(C + (g + 8) * ld + nt * 8 + 2 * t) = make_float2(acc[nt][2], acc[nt][3]);
+  }
+}
 
 // ------------------------------------------------------------------------------------------ prep
 namespace dprep {
@@ -288,7 +344,7 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const int j = chh * 32 + j8 * 8 + e;
-          l[e] = j < i ? nb * __uint_as_float(v[j8 * 8 + e]) * exp2f(g2i - G2[j]) : 0.f;
+          l[e] = j < i ? nb * __uint_as_float(v[j8 * 8 + e]) * ex2(g2i - G2[j]) : 0.f;
         }
         *reinterpret_cast<float4*>(dst + j8 * 8) = make_float4(l[0], l[1], l[2], l[3]);
         *reinterpret_cast<float4*>(dst + j8 * 8 + 4) = make_float4(l[4], l[5], l[6], l[7]);
@@ -301,7 +357,7 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const int j = chh * 32 + j8 * 8 + e;
-          a[e] = j <= i ? __uint_as_float(v[j8 * 8 + e]) * exp2f(g2i - G2[j]) : 0.f;
+          a[e] = j <= i ? __uint_as_float(v[j8 * 8 + e]) * ex2(g2i - G2[j]) : 0.f;
         }
         dst[j8] = pack8(a);
       }
@@ -310,45 +366,52 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
   tc_fence_before();
   __syncthreads();
 
-  // 5. T = (I - L)^-1 in fp32.  5a: diagonal 16x16 blocks, thread (b, c) solves column c of block b
-  //    with the column in registers.
-  if (ok && tid < 64) {
-    const int b0 = (tid >> 4) * 16, c = tid & 15;
-    float col[16];
-#pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      float acc = 0.f;
-      if (r == c) acc = 1.f;
-      if (r > c) {
-        acc = Lf[(b0 + r) * LDF + b0 + c];
-#pragma unroll
-        for (int kx = 0; kx < r; ++kx)
-          if (kx > c) acc = fmaf(Lf[(b0 + r) * LDF + b0 + kx], col[kx], acc);
-      }
-      col[r] = acc;
+  // 5. T = (I - L)^-1 from 16x16 block products on the tensor cores (mma.sync m16n8k8 tf32 with the
+  //    3xTF32 split, fp32-accurate).  Level 0, warp b: T_bb = sum_{k<16} L_bb^k as
+  //    (I + N)(I + N^2)(I + N^4)(I + N^8).  Level d = 1..3, warp j: T_{j+d,j} = T_ii sum_{k=j}^{i-1}
+  //    L_ik T_kj.  Scratch lives in the unused upper blocks of T (level 0) and of L (levels).
+  if (ok && warp < 4) {
+    const int b = warp;
+    float* P = Tf + (16 * b) * LDF + 16 * b;
+    // warp-private scratch: upper blocks (0,1), (1,2), (2,3), (0,3) of T
+    float* Q = Tf + (16 * (b == 3 ? 0 : b)) * LDF + 16 * (b == 3 ? 3 : b + 1);
+    const float* N = Lf + (16 * b) * LDF + 16 * b;
+    for (int e = lane; e < 256; e += 32) {  // P = I + N
+      const int r = e >> 4, c = e & 15;
+      P[r * LDF + c] = N[r * LDF + c] + (r == c ? 1.f : 0.f);
     }
-#pragma unroll
-    for (int r = 0; r < 16; ++r) Tf[(b0 + r) * LDF + b0 + c] = col[r];
+    __syncwarp();
+    const float* Qsrc = N;
+#pragma unroll 1
+    for (int step = 0; step < 3; ++step) {
+      float acc[2][4];
+      bmm16_init(acc, nullptr, 0);
+      bmm16_acc(acc, Qsrc, Qsrc, LDF);  // Q = Q_prev^2 (N^2, N^4, N^8)
+      __syncwarp();
+      bmm16_store(acc, Q, LDF);
+      __syncwarp();
+      Qsrc = Q;
+      bmm16_init(acc, P, LDF);
+      bmm16_acc(acc, P, Q, LDF);        // P += P Q
+      __syncwarp();
+      bmm16_store(acc, P, LDF);
+      __syncwarp();
+    }
   }
   __syncthreads();
-  // 5b. block rows 1..3: T_ij = T_ii * sum_{k=j}^{i-1} L_ik T_kj (M staged in L's upper triangle)
-  for (int bi = 1; bi < 4; ++bi) {
-    if (ok) {
-      for (int e = tid; e < bi * 256; e += THREADS) {
-        const int bj = e >> 8, rr = (e >> 4) & 15, cc = e & 15;
-        float m = 0.f;
-        for (int x = bj * 16; x < bi * 16; ++x) m = fmaf(Lf[(bi * 16 + rr) * LDF + x], Tf[x * LDF + bj * 16 + cc], m);
-        Lf[(bj * 16 + rr) * LDF + bi * 16 + cc] = m;
-      }
-    }
-    __syncthreads();
-    if (ok) {
-      for (int e = tid; e < bi * 256; e += THREADS) {
-        const int bj = e >> 8, rr = (e >> 4) & 15, cc = e & 15;
-        float t = 0.f;
-        for (int x = 0; x <= rr; ++x) t = fmaf(Tf[(bi * 16 + rr) * LDF + bi * 16 + x], Lf[(bj * 16 + x) * LDF + bi * 16 + cc], t);
-        Tf[(bi * 16 + rr) * LDF + bj * 16 + cc] = t;
-      }
+#pragma unroll 1
+  for (int d = 1; d < 4; ++d) {
+    if (ok && warp < 4 - d) {
+      const int j = warp, i = j + d;
+      float* M = Lf + (16 * j) * LDF + 16 * i;  // upper block (j, i) of L as scratch
+      float acc[2][4];
+      bmm16_init(acc, nullptr, 0);
+      for (int k = j; k < i; ++k) bmm16_acc(acc, Lf + (16 * i) * LDF + 16 * k, Tf + (16 * k) * LDF + 16 * j, LDF);
+      bmm16_store(acc, M, LDF);
+      __syncwarp();
+      bmm16_init(acc, nullptr, 0);
+      bmm16_acc(acc, Tf + (16 * i) * LDF + 16 * i, M, LDF);
+      bmm16_store(acc, Tf + (16 * i) * LDF + 16 * j, LDF);
     }
     __syncthreads();
   }
