@@ -139,21 +139,25 @@ gqa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
       // block j+1 while softmax B is still on block j, so the two row groups overlap each other
       // and the tensor pipe instead of taking turns.  Each S commit also covers the PV of the
       // same head issued before it (O rescale and P-tile reuse rely on that).
+      // descriptors built once; a k step adds its byte offset / 16 to the start-address field
+      // (shared-memory addresses stay below 2^18, so the field never carries)
+      const uint64_t dV = sdesc_sw128(base + OFF_V, HALF, 1024);
       auto issue_s = [&](int j, uint32_t q_off, uint32_t tm, uint32_t bar) {
-        const uint32_t kb = base + ((j & 1) ? OFF_K1 : OFF_K0);
+        const uint64_t dq = sdesc_sw128(base + q_off, 16, 1024);
+        const uint64_t dk = sdesc_sw128(base + ((j & 1) ? OFF_K1 : OFF_K0), 16, 1024);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
-          umma_ss(tmem + tm, sdesc_sw128(base + q_off + off, 16, 1024), sdesc_sw128(kb + off, 16, 1024), ID_QK, kk > 0);
+          const uint32_t off = ((kk >> 2) * HALF + (kk & 3) * 32) >> 4;
+          umma_ss(tmem + tm, dq + off, dk + off, ID_QK, kk > 0);
         }
         umma_commit(bar);
       };
       auto issue_pv = [&](int j, uint32_t p_off, uint32_t tm) {
+        const uint64_t dp = sdesc_sw128(base + p_off, 16, 1024);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t aoff = (kk >> 2) * HALF + (kk & 3) * 32;
-          umma_ss(tmem + tm, sdesc_sw128(base + p_off + aoff, 16, 1024),
-                  sdesc_sw128(base + OFF_V + kk * 2048, HALF, 1024), ID_PV, (j > 0 || kk > 0) ? 1u : 0u);
+          const uint32_t aoff = ((kk >> 2) * HALF + (kk & 3) * 32) >> 4;
+          umma_ss(tmem + tm, dp + aoff, dV + (uint32_t)(kk * 2048 >> 4), ID_PV, (j > 0 || kk > 0) ? 1u : 0u);
         }
       };
       bool ok = mbar_wait(bar0 + 8 * B_Q, 0, abort_flag) && mbar_wait(bar0 + 8 * B_KF0, 0, abort_flag);

@@ -506,8 +506,8 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
 //     MMA thread  : vn = S^T W^T (M128 N64 K128); then o^T = S^T Qg^T
 //     state warps : v_new^T = U^T - vn -> bf16 A tile in SMEM; then o^T of chunk n-1 -> out
 //     MMA thread  : S^T += v_new^T Kg (M128 N128 K64, Kg MN-major); then o^T += v_new^T Aqk^T
-//   Warps: 0 TMA producer (and work counter), 1 TMEM allocator + single-thread MMA issuer, 2-5
-//   state warps (one thread per dv row = TMEM lane).  Every mbarrier wait is bounded; a wait that
+//   Warps: 0 TMA producer (and work counter), 1 TMEM allocator + single-thread MMA issuer, 2-9
+//   state warps (two per TMEM lane quarter, each owning half of a dv row's columns).  Every mbarrier wait is bounded; a wait that
 //   runs out sets the device error word, and the CTA drains its copies and MMAs, frees TMEM and
 //   returns.
 namespace drtc {
@@ -518,12 +518,12 @@ constexpr uint32_t ST_W = 0, ST_QG = 2 * KM_HALF, ST_KG = 4 * KM_HALF, ST_A = 6 
                    ST_BYTES = 9 * KM_HALF;           // U^T: [128 dv][128 B]
 constexpr uint32_t OFF_SA = 2 * ST_BYTES;            // S^T bf16 A tile: [2 dk halves][128 dv][128 B]
 constexpr uint32_t OFF_VA = OFF_SA + 2 * 128 * 128;  // v_new^T bf16 A tile: [128 dv][128 B]
-constexpr uint32_t OFF_OST = OFF_VA + 128 * 128;     // o staging: per state warp [64 tok][32 dv] bf16
+constexpr uint32_t OFF_OST = OFF_VA + 128 * 128;     // o staging: per state warp [32 tok][32 dv] bf16
 constexpr uint32_t OFF_META = OFF_OST + 4 * 64 * 32 * 2;
 constexpr uint32_t OFF_BAR = OFF_META + 2 * 32;
 enum { B_FULL0 = 0, B_FULL1, B_EMPTY0, B_EMPTY1, B_SA, B_VN, B_VNEW, B_SDONE, B_ODONE0, B_ODONE1, B_DRAIN, NBAR };
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 8 * NBAR + 16 + 1024;
-constexpr int THREADS = 192;
+constexpr int THREADS = 320;
 constexpr uint32_t TM_S = 0, TM_VN = 128, TM_O = 192, TM_COLS = 512;
 constexpr long long DRAIN_BUDGET = 2000000000LL;
 
@@ -560,7 +560,7 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
   const int H = p.heads;
 
   if (tid == 0) {
-    for (int i = 0; i < NBAR; ++i) mbar_init(bar0 + 8 * i, (i == B_SA || i == B_VNEW) ? 128u : 1u);
+    for (int i = 0; i < NBAR; ++i) mbar_init(bar0 + 8 * i, (i == B_SA || i == B_VNEW) ? 256u : 1u);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -633,6 +633,7 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
       constexpr uint32_t ID_N64 = idesc_bf16(128, 64, false, false);
       constexpr uint32_t ID_N64_BMN = idesc_bf16(128, 64, false, true);
       constexpr uint32_t ID_N128_BMN = idesc_bf16(128, 128, false, true);
+      const uint64_t dSA = sdesc_sw128(base + OFF_SA, 16, 1024), dVA = sdesc_sw128(base + OFF_VA, 16, 1024);
       for (int n = 0;; ++n) {
         const int st = n & 1;
         const uint32_t sb = base + st * ST_BYTES;
@@ -641,12 +642,15 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
         if (!mbar_wait(bar0 + 8 * B_SA, n & 1, abort_flag)) break;
         tc_fence_after();
         const uint32_t tO = tmem + TM_O + 64u * (uint32_t)st;
+        // Descriptors are built once per stage; a k step adds its byte offset / 16 to the start
+        // address field (shared-memory addresses stay below 2^18, so the field never carries).
+        const uint64_t dW = sdesc_sw128(sb + ST_W, KM_HALF, 1024), dQG = sdesc_sw128(sb + ST_QG, 16, 1024),
+                       dKG = sdesc_sw128(sb + ST_KG, KM_HALF, 1024), dA = sdesc_sw128(sb + ST_A, 16, 1024);
         // vn = S^T W^T  (K = 128 dk: 2 swizzle halves x 4 steps of 16; W^T [dk][tok] is MN-major)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t aoff = (uint32_t)(kk >> 2) * (128u * 128u) + (uint32_t)(kk & 3) * 32u;
-          umma_ss(tmem + TM_VN, sdesc_sw128(base + OFF_SA + aoff, 16, 1024),
-                  sdesc_sw128(sb + ST_W + (uint32_t)kk * 2048u, KM_HALF, 1024), ID_N64_BMN, kk > 0 ? 1u : 0u);
+          umma_ss(tmem + TM_VN, dSA + (aoff >> 4), dW + ((uint32_t)kk * 2048u >> 4), ID_N64_BMN, kk > 0 ? 1u : 0u);
         }
         umma_commit(bar0 + 8 * B_VN);
         // o^T = S^T Qg^T
@@ -654,22 +658,19 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t aoff = (uint32_t)(kk >> 2) * (128u * 128u) + (uint32_t)(kk & 3) * 32u;
           const uint32_t boff = (uint32_t)(kk >> 2) * KM_HALF + (uint32_t)(kk & 3) * 32u;
-          umma_ss(tO, sdesc_sw128(base + OFF_SA + aoff, 16, 1024), sdesc_sw128(sb + ST_QG + boff, 16, 1024), ID_N64,
-                  kk > 0 ? 1u : 0u);
+          umma_ss(tO, dSA + (aoff >> 4), dQG + (boff >> 4), ID_N64, kk > 0 ? 1u : 0u);
         }
         if (!mbar_wait(bar0 + 8 * B_VNEW, n & 1, abort_flag)) break;
         tc_fence_after();
         // S^T += v_new^T Kg  (Kg MN-major: [2 dk halves][64 tok][128 B]; K = 64 tokens in 4 steps)
 #pragma unroll
         for (int kt = 0; kt < 4; ++kt)
-          umma_ss(tmem + TM_S, sdesc_sw128(base + OFF_VA + kt * 32, 16, 1024),
-                  sdesc_sw128(sb + ST_KG + kt * 2048, KM_HALF, 1024), ID_N128_BMN, 1u);
+          umma_ss(tmem + TM_S, dVA + (uint32_t)(kt * 32 >> 4), dKG + (uint32_t)(kt * 2048 >> 4), ID_N128_BMN, 1u);
         umma_commit(bar0 + 8 * B_SDONE);
         // o^T += v_new^T Aqk^T
 #pragma unroll
         for (int kt = 0; kt < 4; ++kt)
-          umma_ss(tO, sdesc_sw128(base + OFF_VA + kt * 32, 16, 1024), sdesc_sw128(sb + ST_A + kt * 32, 16, 1024),
-                  ID_N64, 1u);
+          umma_ss(tO, dVA + (uint32_t)(kt * 32 >> 4), dA + (uint32_t)(kt * 32 >> 4), ID_N64, 1u);
         umma_commit(bar0 + 8 * (B_ODONE0 + st));
         umma_commit(bar0 + 8 * (B_EMPTY0 + st));
       }
@@ -679,28 +680,31 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
       mbar_wait(bar0 + 8 * B_DRAIN, 0, &never, DRAIN_BUDGET);
     }
   } else {
-    // ---------------------------------------------------------------- state warps (128 threads)
-    const int q4 = warp & 3;       // the TMEM lane quarter this warp may access
-    const int r = q4 * 32 + lane;  // dv row == TMEM lane
+    // ---------------------------------------------------------------- state warps (256 threads)
+    // Two warps per TMEM lane quarter; warp half `hf` owns half of every row's columns: S^T
+    // columns [64 hf, +64), vn / o columns (tokens) [32 hf, +32).
+    const int q4 = warp & 3;          // the TMEM lane quarter this warp may access
+    const int hf = (warp - 2) >> 2;   // 0 for warps 2-5, 1 for warps 6-9
+    const int r = q4 * 32 + lane;     // dv row == TMEM lane
     const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
-    const uint32_t tS = tmem + lane_addr + TM_S, tVN = tmem + lane_addr + TM_VN, tO = tmem + lane_addr + TM_O;
+    const uint32_t tS = tmem + lane_addr + TM_S + 64 * hf, tVN = tmem + lane_addr + TM_VN + 32 * hf,
+                   tO = tmem + lane_addr + TM_O + 32 * hf;
     uint8_t* sa = gbase + OFF_SA;
     uint8_t* va = gbase + OFF_VA;
-    bf16* ost = reinterpret_cast<bf16*>(gbase + OFF_OST) + q4 * (64 * 32);  // [64 tok][32 dv] of this warp
+    bf16* ost = reinterpret_cast<bf16*>(gbase + OFF_OST) + (hf * 4 + q4) * (32 * 32);  // [32 tok][32 dv]
 
     // o^T of chunk (s, h, c) (complete in TMEM buffer b) -> out[token][h][dv], 64-byte pieces
     auto o_epilogue = [&](int b, int s, int h, int c) {
-      uint32_t o[2][32];
-      tmem_ld32(tO + 64 * b, o[0]);
-      tmem_ld32(tO + 64 * b + 32, o[1]);
+      uint32_t o[32];
+      tmem_ld32(tO + 64 * b, o);
       tmem_ld_wait();
 #pragma unroll
-      for (int t = 0; t < 64; ++t) ost[t * 32 + lane] = __float2bfloat16_rn(__uint_as_float(o[t >> 5][t & 31]));
+      for (int t = 0; t < 32; ++t) ost[t * 32 + lane] = __float2bfloat16_rn(__uint_as_float(o[t]));
       __syncwarp();
-      const int tok0 = p.cu[s] + c * DR_C;
-      const int len = min(DR_C, p.cu[s + 1] - tok0);
+      const int tok0 = p.cu[s] + c * DR_C + 32 * hf;
+      const int len = min(32, p.cu[s + 1] - tok0);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < 4; ++i) {
         const int e = lane + i * 32, tr = e >> 2, ch = e & 3;
         if (tr < len)
           *reinterpret_cast<uint4*>(p.out + ((int64_t)(tok0 + tr) * H + h) * DR_D + q4 * 32 + ch * 8) =
@@ -712,12 +716,13 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
       if (!p.final_state) return;
       const int64_t sh = (int64_t)s * H + h;
 #pragma unroll
-      for (int cb = 0; cb < 4; ++cb) {
+      for (int cb = 0; cb < 2; ++cb) {
         uint32_t v[32];
         tmem_ld32(tS + cb * 32, v);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) p.final_state[(sh * DR_D + cb * 32 + i) * DR_D + r] = __uint_as_float(v[i]);
+        for (int i = 0; i < 32; ++i)
+          p.final_state[(sh * DR_D + 64 * hf + cb * 32 + i) * DR_D + r] = __uint_as_float(v[i]);
       }
     };
 
@@ -742,18 +747,18 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
         }
         const int64_t sh = (int64_t)s * H + h;
 #pragma unroll
-        for (int cb = 0; cb < 4; ++cb) {  // S^T[r][dk] = initial_state[dk][r]
+        for (int cb = 0; cb < 2; ++cb) {  // S^T[r][dk] = initial_state[dk][r]
           uint32_t v[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i)
-            v[i] = __float_as_uint(p.init_state ? p.init_state[(sh * DR_D + cb * 32 + i) * DR_D + r] : 0.f);
+            v[i] = __float_as_uint(p.init_state ? p.init_state[(sh * DR_D + 64 * hf + cb * 32 + i) * DR_D + r] : 0.f);
           tmem_st32(tS + cb * 32, v);
         }
         tmem_st_wait();
       }
       // S^T -> bf16 A tile; S^T *= gamma in TMEM (this chunk's MMAs read the A tile)
 #pragma unroll
-      for (int cb = 0; cb < 4; ++cb) {
+      for (int cb = 0; cb < 2; ++cb) {
         uint32_t v[32];
         tmem_ld32(tS + cb * 32, v);
         tmem_ld_wait();
@@ -762,7 +767,7 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
           float f[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(v[j * 8 + i]);
-          *reinterpret_cast<uint4*>(sa + sw128_off(r, cb * 4 + j, 128)) = pack8(f);
+          *reinterpret_cast<uint4*>(sa + sw128_off(r, hf * 8 + cb * 4 + j, 128)) = pack8(f);
         }
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * gam);
@@ -777,17 +782,16 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
       tc_fence_after();
       {
         const uint8_t* ut = gbase + st * ST_BYTES + ST_UT;
-        uint32_t v[2][32];
-        tmem_ld32(tVN, v[0]);
-        tmem_ld32(tVN + 32, v[1]);
+        uint32_t v[32];
+        tmem_ld32(tVN, v);
         tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < 4; ++j) {
           float u[8], f[8];
-          unpack8(*reinterpret_cast<const uint4*>(ut + sw128_off(r, j, 128)), u);
+          unpack8(*reinterpret_cast<const uint4*>(ut + sw128_off(r, hf * 4 + j, 128)), u);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) f[i] = u[i] - __uint_as_float(v[j >> 2][(j & 3) * 8 + i]);
-          *reinterpret_cast<uint4*>(va + sw128_off(r, j, 128)) = pack8(f);
+          for (int i = 0; i < 8; ++i) f[i] = u[i] - __uint_as_float(v[j * 8 + i]);
+          *reinterpret_cast<uint4*>(va + sw128_off(r, hf * 4 + j, 128)) = pack8(f);
         }
       }
       fence_proxy_async_smem();
