@@ -136,11 +136,22 @@ __device__ __forceinline__ void bmm16_init(float (&acc)[2][4], const float* C, i
     acc[nt][3] = C ? C[(g + 8) * ld + nt * 8 + 2 * t + 1] : 0.f;
   }
 }
-// acc += X Y (16x16 each)
+// acc += X Y (16x16 each).  The three split terms and the two k halves accumulate into
+// independent partial tiles, so the dependent mma chain is two deep instead of twelve.
 __device__ __forceinline__ void bmm16_acc(float (&acc)[2][4], const float* X, const float* Y, int ld) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  float part[2][3][2][4];
 #pragma unroll
-  for (int k0 = 0; k0 < 16; k0 += 8) {
+  for (int k = 0; k < 2; ++k)
+#pragma unroll
+    for (int q = 0; q < 3; ++q)
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) part[k][q][nt][e] = 0.f;
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int k0 = 8 * k;
     uint32_t ah[4], al[4];
     tf32_split(X[g * ld + k0 + t], ah[0], al[0]);
     tf32_split(X[(g + 8) * ld + k0 + t], ah[1], al[1]);
@@ -151,11 +162,17 @@ __device__ __forceinline__ void bmm16_acc(float (&acc)[2][4], const float* X, co
       uint32_t bh0, bl0, bh1, bl1;
       tf32_split(Y[(k0 + t) * ld + nt * 8 + g], bh0, bl0);
       tf32_split(Y[(k0 + t + 4) * ld + nt * 8 + g], bh1, bl1);
-      mma_tf32(acc[nt], al, bh0, bh1);
-      mma_tf32(acc[nt], ah, bl0, bl1);
-      mma_tf32(acc[nt], ah, bh0, bh1);
+      mma_tf32(part[k][0][nt], al, bh0, bh1);
+      mma_tf32(part[k][1][nt], ah, bl0, bl1);
+      mma_tf32(part[k][2][nt], ah, bh0, bh1);
     }
   }
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      acc[nt][e] += ((part[0][0][nt][e] + part[1][0][nt][e]) + (part[0][1][nt][e] + part[1][1][nt][e])) +
+                    (part[0][2][nt][e] + part[1][2][nt][e]);
 }
 __device__ __forceinline__ void bmm16_store(const float (&acc)[2][4], float* C, int ld) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
@@ -366,55 +383,71 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
   tc_fence_before();
   __syncthreads();
 
-  // 5. T = (I - L)^-1 from 16x16 block products on the tensor cores (mma.sync m16n8k8 tf32 with the
-  //    3xTF32 split, fp32-accurate).  Level 0, warp b: T_bb = sum_{k<16} L_bb^k as
-  //    (I + N)(I + N^2)(I + N^4)(I + N^8).  Level d = 1..3, warp j: T_{j+d,j} = T_ii sum_{k=j}^{i-1}
-  //    L_ik T_kj.  Scratch lives in the unused upper blocks of T (level 0) and of L (levels).
-  if (ok && warp < 4) {
-    const int b = warp;
-    float* P = Tf + (16 * b) * LDF + 16 * b;
-    // warp-private scratch: upper blocks (0,1), (1,2), (2,3), (0,3) of T
-    float* Q = Tf + (16 * (b == 3 ? 0 : b)) * LDF + 16 * (b == 3 ? 3 : b + 1);
-    const float* N = Lf + (16 * b) * LDF + 16 * b;
-    for (int e = lane; e < 256; e += 32) {  // P = I + N
-      const int r = e >> 4, c = e & 15;
-      P[r * LDF + c] = N[r * LDF + c] + (r == c ? 1.f : 0.f);
+  // 5. T = (I - L)^-1 in fp32.
+  //    Level 0 (warps 0-1, half a warp per diagonal block, lane = row): T_bb by row substitution
+  //    T_r = e_r + sum_{j<r} N_rj T_j with row j broadcast by shuffles once it is final.
+  //    Levels 1-3: 16x16 block products on the tensor cores (mma.sync tf32, 3xTF32 split,
+  //    fp32-accurate): T_10 = T_11 L_10 T_00 and T_32 = T_33 L_32 T_22; then the 32x32 corner
+  //    T_[23][01] = T_[23][23] (L_[23][01] T_[01][01]) as X = L T then Y = T X, four blocks each.
+  //    Scratch: the unused upper blocks of L.
+  if (ok && warp < 2) {
+    const int b = 2 * warp + (lane >> 4), r = lane & 15;
+    const float* nrow = Lf + (16 * b + r) * LDF + 16 * b;
+    float n[16], t[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      n[k] = nrow[k];
+      t[k] = k == r ? 1.f : 0.f;
     }
-    __syncwarp();
-    const float* Qsrc = N;
-#pragma unroll 1
-    for (int step = 0; step < 3; ++step) {
-      float acc[2][4];
-      bmm16_init(acc, nullptr, 0);
-      bmm16_acc(acc, Qsrc, Qsrc, LDF);  // Q = Q_prev^2 (N^2, N^4, N^8)
-      __syncwarp();
-      bmm16_store(acc, Q, LDF);
-      __syncwarp();
-      Qsrc = Q;
-      bmm16_init(acc, P, LDF);
-      bmm16_acc(acc, P, Q, LDF);        // P += P Q
-      __syncwarp();
-      bmm16_store(acc, P, LDF);
-      __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 15; ++j) {
+      const int src = (lane & 16) | j;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const float tj = __shfl_sync(0xffffffffu, t[k], src);
+        if (r > j) t[k] = fmaf(n[j], tj, t[k]);
+      }
     }
+    float* trow = Tf + (16 * b + r) * LDF + 16 * b;
+#pragma unroll
+    for (int k = 0; k < 16; k += 4) *reinterpret_cast<float4*>(trow + k) = make_float4(t[k], t[k + 1], t[k + 2], t[k + 3]);
   }
   __syncthreads();
-#pragma unroll 1
-  for (int d = 1; d < 4; ++d) {
-    if (ok && warp < 4 - d) {
-      const int j = warp, i = j + d;
-      float* M = Lf + (16 * j) * LDF + 16 * i;  // upper block (j, i) of L as scratch
-      float acc[2][4];
-      bmm16_init(acc, nullptr, 0);
-      for (int k = j; k < i; ++k) bmm16_acc(acc, Lf + (16 * i) * LDF + 16 * k, Tf + (16 * k) * LDF + 16 * j, LDF);
-      bmm16_store(acc, M, LDF);
-      __syncwarp();
-      bmm16_init(acc, nullptr, 0);
-      bmm16_acc(acc, Tf + (16 * i) * LDF + 16 * i, M, LDF);
-      bmm16_store(acc, Tf + (16 * i) * LDF + 16 * j, LDF);
-    }
-    __syncthreads();
+  auto blk = [&](float* base_, int bi, int bj) { return base_ + (16 * bi) * LDF + 16 * bj; };
+  // level 1: warp 0 -> T_10, warp 1 -> T_32
+  if (ok && warp < 2) {
+    const int j = 2 * warp, i = j + 1;
+    float acc[2][4];
+    bmm16_init(acc, nullptr, 0);
+    bmm16_acc(acc, blk(Lf, i, j), blk(Tf, j, j), LDF);
+    float* M = blk(Lf, j, i);
+    bmm16_store(acc, M, LDF);
+    __syncwarp();
+    bmm16_init(acc, nullptr, 0);
+    bmm16_acc(acc, blk(Tf, i, i), M, LDF);
+    bmm16_store(acc, blk(Tf, i, j), LDF);
   }
+  __syncthreads();
+  // level 2: X_ij (i in {2,3}, j in {0,1}) = L_i0 T_0j + L_i1 T_1j (T_01 = 0) into L's block (j, i)
+  if (ok && warp < 4) {
+    const int i = 2 + (warp >> 1), j = warp & 1;
+    float acc[2][4];
+    bmm16_init(acc, nullptr, 0);
+    if (j == 0) bmm16_acc(acc, blk(Lf, i, 0), blk(Tf, 0, 0), LDF);
+    bmm16_acc(acc, blk(Lf, i, 1), blk(Tf, 1, j), LDF);
+    bmm16_store(acc, blk(Lf, j, i), LDF);
+  }
+  __syncthreads();
+  // level 3: T_ij = T_i2 X_2j + T_i3 X_3j (T_23 = 0)
+  if (ok && warp < 4) {
+    const int i = 2 + (warp >> 1), j = warp & 1;
+    float acc[2][4];
+    bmm16_init(acc, nullptr, 0);
+    bmm16_acc(acc, blk(Tf, i, 2), blk(Lf, j, 2), LDF);
+    if (i == 3) bmm16_acc(acc, blk(Tf, 3, 3), blk(Lf, j, 3), LDF);
+    bmm16_store(acc, blk(Tf, i, j), LDF);
+  }
+  __syncthreads();
 
   // 6. TU = bf16(T diag(beta)), TW = bf16(T diag(beta e^G)) as K-major swizzled B tiles (over L)
   if (ok) {
