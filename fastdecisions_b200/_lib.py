@@ -34,6 +34,8 @@ SIGNATURES = {
                                              vp, vp, vp, vp, sz, vp]),
     "fdk_chunk_gated_delta_rule_fwd_noalloc": (i32, [vp, vp, i64, vp, i64, vp, vp, vp, i64, i64, i64, i64, i64,
                                                      f32, vp, vp, vp, vp]),
+    "fdk_gdn_fused_delta_rule_fwd": (i32, [vp, i64, vp, i32, i64, i64, i64, i64, vp, vp, vp, i64, i64, i64, f32, vp,
+                                           vp, vp, vp, sz, vp]),
     "fdk_gated_rmsnorm": (i32, [vp, vp, i64, vp, i32, vp, i64, i64, i64, f32, vp]),
     "fdk_attn_qk_norm_rope": (i32, [vp, i64, vp, vp, i32, vp, vp, i64, i32, vp, vp, i64, i64, i64, i64, f32, vp]),
     "fdk_gqa_fwd": (i32, [vp, i64, vp, i64, vp, i64, vp, i64, i64, i64, i64, i64, i64, f32, vp, i64, i32, vp, vp]),
@@ -81,7 +83,8 @@ def poll_device_error() -> int:
 
 
 # kernels each compute entry point launches (used to count device launches in a timed region)
-KERNELS_PER_CALL = {"fdk_chunk_gated_delta_rule_fwd": 3, "fdk_chunk_gated_delta_rule_fwd_noalloc": 3}
+KERNELS_PER_CALL = {"fdk_chunk_gated_delta_rule_fwd": 3, "fdk_chunk_gated_delta_rule_fwd_noalloc": 3,
+                    "fdk_gdn_fused_delta_rule_fwd": 3}
 call_counts: dict = {}
 
 

@@ -18,6 +18,7 @@
 //        v_new^T = U^T - S^T W^T ;  o^T = S^T Qg^T + v_new^T Aqk^T ;  S^T = gamma S^T + v_new^T Kg
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <string.h>
 
 #include "common.cuh"
 #include "mma_sm80.cuh"
@@ -43,22 +44,23 @@ struct WsLayout {
   int64_t max_chunks;
 };
 
-// chunk table [nseg + 1] + work counter, chunk info (first token, length) [max_chunks], tiles
+// chunk table [nseg + 1] + work counter, chunk info (first token, length, segment start)
+// [max_chunks], tiles
 __host__ __device__ inline WsLayout ws_layout(int64_t tokens, int64_t nseg, int64_t heads) {
   WsLayout l;
   l.max_chunks = (tokens + DR_C - 1) / DR_C + nseg;
   l.off_table = 0;
   l.off_info = align256((size_t)(nseg + 2) * 4);
-  l.off_tiles = l.off_info + align256((size_t)l.max_chunks * 8);
+  l.off_tiles = l.off_info + align256((size_t)l.max_chunks * 16);
   l.total = l.off_tiles + align256((size_t)l.max_chunks * heads * CH_BYTES);
   return l;
 }
 
 // One CTA of 256 threads: exclusive scan of ceil(len / 64) over segments (table[s] = first chunk
-// of segment s, table[nseg] = chunk count), each chunk's (first token, length), and the zeroed
+// of segment s, table[nseg] = chunk count), each chunk's (first token, length, segment start), and the zeroed
 // work counter of the recurrence (table[nseg + 1]).
 __global__ void __launch_bounds__(256) chunk_table_kernel(const int32_t* __restrict__ cu, int nseg,
-                                                          int32_t* __restrict__ table, int2* __restrict__ info) {
+                                                          int32_t* __restrict__ table, int4* __restrict__ info) {
   __shared__ int warp_sums[8];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int carry = 0;
@@ -87,7 +89,7 @@ __global__ void __launch_bounds__(256) chunk_table_kernel(const int32_t* __restr
     const int first = carry + woff + incl - n;
     if (s < nseg) {
       table[s] = first;
-      for (int c = 0; c < n; ++c) info[first + c] = make_int2(t0 + c * DR_C, min(DR_C, len - c * DR_C));
+      for (int c = 0; c < n; ++c) info[first + c] = make_int4(t0 + c * DR_C, min(DR_C, len - c * DR_C), t0, 0);
     }
     carry += total;
     __syncthreads();  // warp_sums is rewritten by the next pass
@@ -201,11 +203,79 @@ constexpr uint32_t TM_D1 = 0, TM_U = 64, TM_W = 0, TM_COLS = 128;
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr long long DRAIN_BUDGET = 2000000000LL;
 
+// Inputs of the prep.  Plain: q / k / v through the tensor maps, g (fp32) and beta (bf16) [T, H].
+// CONV (the fused GDN prologue): the [T, >= C] projection itself -- q / k / v come from the
+// depthwise causal conv (width 4) + SiLU of its first C = 2 key_dim + value_dim columns, g and
+// beta from its a / b columns (g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b)), with
+// the same arithmetic and bf16 roundings as the packed-conv and gate kernels.
+struct PrepIn {
+  const float* g;
+  const bf16* beta;
+  const bf16* proj;
+  int64_t ld;
+  const bf16* conv_w;  // [C][4]
+  int key_dim;
+  int a_col, b_col;
+  const float* A_log;
+  const float* dt_bias;
+  int64_t tokens;
+};
+
+// conv + SiLU of one 8-channel group over `rows` consecutive tokens starting at t, written as bf16
+// into a 128-byte-swizzled row of A1 (row base srow0, 16-byte chunk c16).  Rows before the segment
+// start read as zero (causal history restarts per segment); rows at or past `tokens` are zero.
+template <int ROWS>
+__device__ __forceinline__ void conv_rows(const PrepIn& in, int64_t col, int64_t t, int64_t seg_start, uint8_t* a1,
+                                          int srow0, int c16) {
+  uint4 x[ROWS + 3];
+#pragma unroll
+  for (int i = 0; i < ROWS + 3; ++i) {
+    const int64_t tt = t - 3 + i;
+    x[i] = (tt >= seg_start && tt < in.tokens) ? __ldg(reinterpret_cast<const uint4*>(in.proj + tt * in.ld + col))
+                                               : make_uint4(0u, 0u, 0u, 0u);
+  }
+  float w[4][8];
+  {
+    const uint4* wp = reinterpret_cast<const uint4*>(in.conv_w + col * 4);  // 8 channels x 4 taps, contiguous
+    float f[8];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      unpack8(__ldg(wp + q), f);  // channels 2q, 2q+1, taps 0..3 each
+#pragma unroll
+      for (int e = 0; e < 8; ++e) w[e & 3][2 * q + (e >> 2)] = f[e];
+    }
+  }
+  float h0[8], h1[8], h2[8];
+  unpack8(x[0], h0);
+  unpack8(x[1], h1);
+  unpack8(x[2], h2);
+#pragma unroll
+  for (int i = 0; i < ROWS; ++i) {
+    float cur[8], y[8];
+    unpack8(x[i + 3], cur);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      float acc = w[3][c] * cur[c];
+      acc = fmaf(w[2][c], h2[c], acc);
+      acc = fmaf(w[1][c], h1[c], acc);
+      acc = fmaf(w[0][c], h0[c], acc);
+      y[c] = silu_tanh(acc);
+    }
+    *reinterpret_cast<uint4*>(a1 + sw128_off(srow0 + i, c16, 128)) = pack8(y);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      h0[c] = h1[c];
+      h1[c] = h2[c];
+      h2[c] = cur[c];
+    }
+  }
+}
+
+template <bool CONV>
 __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
     const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
-    const __grid_constant__ CUtensorMap mv, const float* __restrict__ g, const bf16* __restrict__ beta,
-    const int2* __restrict__ info, const int32_t* __restrict__ table, int nseg, int heads, float scale,
-    uint8_t* __restrict__ tiles) {
+    const __grid_constant__ CUtensorMap mv, const PrepIn in, const int4* __restrict__ info,
+    const int32_t* __restrict__ table, int nseg, int heads, float scale, uint8_t* __restrict__ tiles) {
   extern __shared__ uint8_t smem_raw[];
   const int ci = blockIdx.x, h = blockIdx.y;
   if (ci >= table[nseg]) return;  // CTA-uniform, before any barrier or TMEM use
@@ -221,8 +291,8 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sb + BARS + 8 * NBAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sb + BARS + 8 * NBAR + 4);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int2 inf = info[ci];
-  const int t0 = inf.x, len = inf.y;
+  const int4 inf = info[ci];
+  const int t0 = inf.x, len = inf.y, seg_start = inf.z;
   uint8_t* tile = tiles + ((size_t)ci * heads + h) * CH_BYTES;
 
   if (tid == 0) {
@@ -242,7 +312,7 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
 
   // 1. raw k rows -> A1 rows 0-63, raw q rows -> rows 64-127 (TMA, 128-byte swizzle; rows past
   //    the end of the tokens read as zero, rows of the next segment are masked below)
-  if (tid == 0) {
+  if (!CONV && tid == 0) {
     prefetch_tmap(&mq);
     prefetch_tmap(&mk);
     prefetch_tmap(&mv);
@@ -257,8 +327,22 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
   if (warp == 1) {
     const int r0 = 2 * lane, r1 = 2 * lane + 1;
     float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
-    if (r0 < len) { a0 = g[(int64_t)(t0 + r0) * heads + h]; b0 = __bfloat162float(beta[(int64_t)(t0 + r0) * heads + h]); }
-    if (r1 < len) { a1 = g[(int64_t)(t0 + r1) * heads + h]; b1 = __bfloat162float(beta[(int64_t)(t0 + r1) * heads + h]); }
+    if (CONV) {  // gates from the projection's a / b columns
+      const float el = -expf(in.A_log[h]), dtb = in.dt_bias[h];
+      if (r0 < len) {
+        const bf16* row = in.proj + (int64_t)(t0 + r0) * in.ld;
+        a0 = el * softplusf_(__bfloat162float(row[in.a_col + h]) + dtb);
+        b0 = round_bf16(sigmoidf_(__bfloat162float(row[in.b_col + h])));
+      }
+      if (r1 < len) {
+        const bf16* row = in.proj + (int64_t)(t0 + r1) * in.ld;
+        a1 = el * softplusf_(__bfloat162float(row[in.a_col + h]) + dtb);
+        b1 = round_bf16(sigmoidf_(__bfloat162float(row[in.b_col + h])));
+      }
+    } else {
+      if (r0 < len) { a0 = in.g[(int64_t)(t0 + r0) * heads + h]; b0 = __bfloat162float(in.beta[(int64_t)(t0 + r0) * heads + h]); }
+      if (r1 < len) { a1 = in.g[(int64_t)(t0 + r1) * heads + h]; b1 = __bfloat162float(in.beta[(int64_t)(t0 + r1) * heads + h]); }
+    }
     const float pair = a0 + a1;
     float incl = pair;
 #pragma unroll
@@ -275,7 +359,14 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
     fw[r1] = b1 * expf(G1);
     if (lane == 31) *reinterpret_cast<float*>(tile + OFF_GAMMA) = expf(G1);
   }
-  bool ok = mbar_wait(bar0 + 8 * B_QK, 0, abort_flag);
+  if (CONV) {  // q (A1 rows 64-127) and k (rows 0-63): thread = 8 channels x 8 tokens, in two runs of 4
+    const int g8 = tid & 31, rs = tid >> 5;
+    const bool isk = g8 >= 16;
+    const int64_t col = (isk ? in.key_dim : 0) + (int64_t)h * DR_D + (g8 & 15) * 8;
+    conv_rows<4>(in, col, (int64_t)t0 + rs * 8, seg_start, sb + A1, (isk ? 0 : 64) + rs * 8, g8 & 15);
+    conv_rows<4>(in, col, (int64_t)t0 + rs * 8 + 4, seg_start, sb + A1, (isk ? 0 : 64) + rs * 8 + 4, g8 & 15);
+  }
+  bool ok = CONV ? true : mbar_wait(bar0 + 8 * B_QK, 0, abort_flag);
   ok = __syncthreads_and(ok) != 0;  // also publishes G2 / beta / fw
 
   if (ok) {
@@ -336,7 +427,13 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
   if (ok) ok = warp_wait(bar0 + 8 * B_MMA1, 0, abort_flag);
   if (ok) tc_fence_after();
   // V rows -> A1 rows 64-127 (q^ is no longer read), landing while the solve runs
-  if (ok && tid == 0) {
+  if (CONV && ok) {  // v by conv: thread = 8 channels x 4 tokens
+    const int g8 = tid & 15, rs = tid >> 4;
+    conv_rows<4>(in, 2 * (int64_t)in.key_dim + (int64_t)h * DR_D + g8 * 8, (int64_t)t0 + rs * 4, seg_start, sb + A1,
+                 64 + rs * 4, g8);
+    fence_proxy_async_smem();
+  }
+  if (!CONV && ok && tid == 0) {
     mbar_expect_tx(bar0 + 8 * B_V, 2 * 8192);
     tma_load_2d(base + A1 + 8192, &mv, bar0 + 8 * B_V, h * DR_D, t0);
     tma_load_2d(base + A1 + 16384 + 8192, &mv, bar0 + 8 * B_V, h * DR_D + 64, t0);
@@ -474,7 +571,7 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
 
   // 7. U^T = V^T TU^T and W^T = K^T TW^T  (M128 N64 K64; A = V / K^ MN-major, B = TU / TW K-major)
   if (ok && tid == 0) {
-    if (mbar_wait(bar0 + 8 * B_V, 0, abort_flag)) {
+    if (CONV || mbar_wait(bar0 + 8 * B_V, 0, abort_flag)) {
       tc_fence_after();
       constexpr uint32_t ID = idesc_bf16(128, 64, true, false);
 #pragma unroll
@@ -511,7 +608,7 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
   // shared memory are released
   if (tid == 0 && *abort_flag) {
     volatile int never = 0;
-    mbar_wait(bar0 + 8 * B_QK, 0, &never, DRAIN_BUDGET);
+    if (!CONV) mbar_wait(bar0 + 8 * B_QK, 0, &never, DRAIN_BUDGET);
     if (issued_v) mbar_wait(bar0 + 8 * B_V, 0, &never, DRAIN_BUDGET);
     if (issued_mma) {  // every MMA this thread issued has completed
       umma_commit(bar0 + 8 * B_DRAIN);
@@ -964,6 +1061,58 @@ extern "C" size_t fdk_chunk_gated_delta_rule_workspace_size(int64_t tokens, int6
   return ws_layout(tokens, num_segments, heads).total;
 }
 
+// Table, prep (plain or with the fused conv + gate prologue) and recurrence.  `q / k / v` are used
+// by the plain prep only; the caller has validated everything.
+static int run_delta_rule(bool conv, const void* q, const void* k, int64_t ld_qk, const void* v, int64_t ld_v,
+                          const dprep::PrepIn& in, const int32_t* cu_seqlens, int64_t num_segments, int64_t tokens,
+                          int64_t heads, float scale, const float* initial_state, void* out, float* final_state,
+                          void* workspace, size_t workspace_bytes, cudaStream_t s) {
+  const WsLayout lay = ws_layout(tokens, num_segments, heads);
+  if (workspace_bytes < lay.total)
+    return set_error(FDK_ERR_INVALID_ARGUMENT, "chunk_gated_delta_rule: workspace %zu bytes < required %zu", workspace_bytes, lay.total);
+  if (lay.max_chunks > 0x7fffffff) return set_error(FDK_ERR_UNSUPPORTED, "chunk_gated_delta_rule: too many chunks");
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int32_t* table = reinterpret_cast<int32_t*>(ws + lay.off_table);
+  int4* info = reinterpret_cast<int4*>(ws + lay.off_info);
+  uint8_t* tiles = ws + lay.off_tiles;
+  const int nseg = (int)num_segments;
+  chunk_table_kernel<<<1, 256, 0, s>>>(cu_seqlens, nseg, table, info);
+  if (int st = check_launch("chunk_gated_delta_rule/table")) return st;
+  if (tokens == 0 && !final_state) return FDK_OK;
+  if (tokens > 0) {
+    CUtensorMap mq, mk, mv;
+    if (conv) {  // the conv prologue reads the projection directly; the maps are never used
+      memset(&mq, 0, sizeof(mq));
+      memset(&mk, 0, sizeof(mk));
+      memset(&mv, 0, sizeof(mv));
+    } else {
+      if (int st = drtc::act_map(&mq, q, tokens, heads, ld_qk)) return st;
+      if (int st = drtc::act_map(&mk, k, tokens, heads, ld_qk)) return st;
+      if (int st = drtc::act_map(&mv, v, tokens, heads, ld_v)) return st;
+    }
+    static bool attr_set[2][64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !attr_set[conv][dev]) {
+      if (conv)
+        cudaFuncSetAttribute(dprep::delta_prep_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dprep::SMEM_BYTES);
+      else
+        cudaFuncSetAttribute(dprep::delta_prep_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dprep::SMEM_BYTES);
+      if (dev >= 0 && dev < 64) attr_set[conv][dev] = true;
+    }
+    const dim3 grid((unsigned)lay.max_chunks, (unsigned)heads);
+    if (conv)
+      dprep::delta_prep_kernel<true><<<grid, dprep::THREADS, dprep::SMEM_BYTES, s>>>(mq, mk, mv, in, info, table, nseg,
+                                                                                   (int)heads, scale, tiles);
+    else
+      dprep::delta_prep_kernel<false><<<grid, dprep::THREADS, dprep::SMEM_BYTES, s>>>(mq, mk, mv, in, info, table, nseg,
+                                                                                    (int)heads, scale, tiles);
+    if (int st = check_launch("chunk_gated_delta_rule/prep")) return st;
+  }
+  return launch_recur(nseg, (int)heads, lay.max_chunks * heads, s, cu_seqlens, table, table + nseg + 1, tiles,
+                      initial_state, static_cast<bf16*>(out), final_state);
+}
+
 extern "C" int fdk_chunk_gated_delta_rule_fwd(const void* q, const void* k, int64_t ld_qk, const void* v, int64_t ld_v,
                                               const float* g, const void* beta, const int32_t* cu_seqlens,
                                               int64_t num_segments, int64_t tokens, int64_t heads, int64_t dk, int64_t dv,
@@ -980,37 +1129,45 @@ extern "C" int fdk_chunk_gated_delta_rule_fwd(const void* q, const void* k, int6
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || ld_qk % 8 || ld_v % 8 ||
       (reinterpret_cast<uintptr_t>(workspace) & 255))
     return set_error(FDK_ERR_ALIGNMENT, "chunk_gated_delta_rule: 16-byte tensors and a 256-byte aligned workspace required");
-  const WsLayout lay = ws_layout(tokens, num_segments, heads);
-  if (workspace_bytes < lay.total)
-    return set_error(FDK_ERR_INVALID_ARGUMENT, "chunk_gated_delta_rule: workspace %zu bytes < required %zu", workspace_bytes, lay.total);
-  if (lay.max_chunks > 0x7fffffff) return set_error(FDK_ERR_UNSUPPORTED, "chunk_gated_delta_rule: too many chunks");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
-  int32_t* table = reinterpret_cast<int32_t*>(ws + lay.off_table);
-  int2* info = reinterpret_cast<int2*>(ws + lay.off_info);
-  uint8_t* tiles = ws + lay.off_tiles;
-  const int nseg = (int)num_segments;
-  chunk_table_kernel<<<1, 256, 0, s>>>(cu_seqlens, nseg, table, info);
-  if (int st = check_launch("chunk_gated_delta_rule/table")) return st;
-  if (tokens == 0 && !final_state) return FDK_OK;
-  if (tokens > 0) {
-    CUtensorMap mq, mk, mv;
-    if (int st = drtc::act_map(&mq, q, tokens, heads, ld_qk)) return st;
-    if (int st = drtc::act_map(&mk, k, tokens, heads, ld_qk)) return st;
-    if (int st = drtc::act_map(&mv, v, tokens, heads, ld_v)) return st;
-    static bool attr_set[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-      cudaFuncSetAttribute(dprep::delta_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dprep::SMEM_BYTES);
-      if (dev >= 0 && dev < 64) attr_set[dev] = true;
-    }
-    dprep::delta_prep_kernel<<<dim3((unsigned)lay.max_chunks, (unsigned)heads), dprep::THREADS, dprep::SMEM_BYTES, s>>>(
-        mq, mk, mv, g, static_cast<const bf16*>(beta), info, table, nseg, (int)heads, scale, tiles);
-    if (int st = check_launch("chunk_gated_delta_rule/prep")) return st;
-  }
-  return launch_recur(nseg, (int)heads, lay.max_chunks * heads, s, cu_seqlens, table, table + nseg + 1, tiles,
-                      initial_state, static_cast<bf16*>(out), final_state);
+  dprep::PrepIn in{};
+  in.g = g;
+  in.beta = static_cast<const bf16*>(beta);
+  return run_delta_rule(false, q, k, ld_qk, v, ld_v, in, cu_seqlens, num_segments, tokens, heads, scale, initial_state,
+                        out, final_state, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int fdk_gdn_fused_delta_rule_fwd(const void* proj, int64_t ld_proj, const void* conv_weight, int kernel_width,
+                                            int64_t key_dim, int64_t value_dim, int64_t a_col, int64_t b_col,
+                                            const float* A_log, const float* dt_bias, const int32_t* cu_seqlens,
+                                            int64_t num_segments, int64_t tokens, int64_t heads, float scale,
+                                            const float* initial_state, void* out, float* final_state, void* workspace,
+                                            size_t workspace_bytes, void* stream) {
+  if (int st = check_device()) return st;
+  if (!proj || !conv_weight || !A_log || !dt_bias || !cu_seqlens || !out || !workspace)
+    return set_error(FDK_ERR_INVALID_ARGUMENT, "gdn_fused_delta_rule: null pointer");
+  if (kernel_width != 4) return set_error(FDK_ERR_UNSUPPORTED, "gdn_fused_delta_rule: kernel_width=%d (4 supported)", kernel_width);
+  if (num_segments < 1 || tokens < 0 || heads < 1 || heads > 65535 || num_segments > 0x7fffffff)
+    return set_error(FDK_ERR_INVALID_ARGUMENT, "gdn_fused_delta_rule: bad sizes");
+  if (key_dim != heads * DR_D || value_dim != heads * DR_D)
+    return set_error(FDK_ERR_UNSUPPORTED, "gdn_fused_delta_rule: key_dim and value_dim must be heads x 128");
+  const int64_t C = 2 * key_dim + value_dim;
+  if (a_col < C || b_col < C || a_col + heads > ld_proj || b_col + heads > ld_proj || ld_proj < C)
+    return set_error(FDK_ERR_INVALID_ARGUMENT, "gdn_fused_delta_rule: a / b columns outside the projection row");
+  if (!aligned16(proj) || ld_proj % 8 || !aligned16(conv_weight) || !aligned16(out) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return set_error(FDK_ERR_ALIGNMENT, "gdn_fused_delta_rule: 16-byte tensors and a 256-byte aligned workspace required");
+  dprep::PrepIn in{};
+  in.proj = static_cast<const bf16*>(proj);
+  in.ld = ld_proj;
+  in.conv_w = static_cast<const bf16*>(conv_weight);
+  in.key_dim = (int)key_dim;
+  in.a_col = (int)a_col;
+  in.b_col = (int)b_col;
+  in.A_log = A_log;
+  in.dt_bias = dt_bias;
+  in.tokens = tokens;
+  return run_delta_rule(true, nullptr, nullptr, 0, nullptr, 0, in, cu_seqlens, num_segments, tokens, heads, scale,
+                        initial_state, out, final_state, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 // ---------------------------------------------------------------------------------------------

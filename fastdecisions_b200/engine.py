@@ -88,10 +88,13 @@ def plan_batches(lengths: Sequence[int], max_tokens: int) -> list:
 
 class DecisionEngine:
     def __init__(self, cfg: ModelConfig, weights: dict, device="cuda", letter_ids=LETTER_IDS,
-                 temperature: float = 1.0, residual_fp32: bool = True):
+                 temperature: float = 1.0, residual_fp32: bool = True, fuse_gdn_prologue: bool = True):
         """``residual_fp32`` keeps the residual stream in float32 (the sum of the layer outputs is
-        never rounded); with False it is stored in bf16 like the eager bf16 model."""
+        never rounded); with False it is stored in bf16 like the eager bf16 model.
+        ``fuse_gdn_prologue`` runs the Gated-DeltaNet conv, gates and delta rule as one call on the
+        projection (same results as the three separate ops, without their HBM round trips)."""
         self.cfg = cfg
+        self.fuse_gdn_prologue = bool(fuse_gdn_prologue)
         self.residual_fp32 = bool(residual_fp32)
         self.dev = torch.device(device)
         self.temperature = float(temperature)
@@ -180,14 +183,20 @@ class DecisionEngine:
         if L.kind == "linear_attention":
             with tm("gemm"):
                 proj = torch.matmul(x, L.w_in.t())                                       # [T, C + vd + 2 Hv]
-            with tm("packed_conv"):
-                q, k, v = ops.packed_conv_qkv(proj[:, :C].unsqueeze(0), L.conv, kd, vd, Dk, cu)
-            with tm("gdn_gates"):
-                g, beta = ops.gdn_gates(proj[:, C + vd + Hv:C + vd + 2 * Hv], proj[:, C + vd:C + vd + Hv],
-                                        L.A_log, L.dt_bias)
-            with tm("delta_rule"):
-                o, _ = ops.chunk_gated_delta_rule(q, k, v, g.unsqueeze(0), beta.unsqueeze(0), cu_seqlens=cu,
-                                                  workspace=ws)
+            if self.fuse_gdn_prologue and Hk == Hv and Dk == Dv == 128:
+                # conv + SiLU, gates and the chunked delta rule in one call on the projection
+                with tm("delta_rule"):
+                    o = ops.gdn_fused_delta_rule(proj, L.conv, L.A_log, L.dt_bias, Hv, C + vd + Hv, C + vd, cu,
+                                                 workspace=ws)
+            else:
+                with tm("packed_conv"):
+                    q, k, v = ops.packed_conv_qkv(proj[:, :C].unsqueeze(0), L.conv, kd, vd, Dk, cu)
+                with tm("gdn_gates"):
+                    g, beta = ops.gdn_gates(proj[:, C + vd + Hv:C + vd + 2 * Hv], proj[:, C + vd:C + vd + Hv],
+                                            L.A_log, L.dt_bias)
+                with tm("delta_rule"):
+                    o, _ = ops.chunk_gated_delta_rule(q, k, v, g.unsqueeze(0), beta.unsqueeze(0), cu_seqlens=cu,
+                                                      workspace=ws)
             with tm("gated_rmsnorm"):
                 on = ops.gated_rmsnorm(o.view(T, Hv, Dv), proj[:, C:C + vd], L.gnorm, c.rms_norm_eps)
             with tm("gemm"):

@@ -20,8 +20,8 @@ from . import ops
 from .engine import plan_batches
 from .workloads import ModelConfig, config5_requests
 
-OPS = ("delta_rule", "gqa_attention", "packed_conv", "qk_norm_rope", "gated_rmsnorm", "residual_rmsnorm", "swiglu",
-       "gdn_gates")
+OPS = ("gdn_fused", "delta_rule", "gqa_attention", "packed_conv", "qk_norm_rope", "gated_rmsnorm", "residual_rmsnorm",
+       "swiglu", "gdn_gates")
 
 
 def _peaks() -> dict:
@@ -63,6 +63,15 @@ def make_case(op: str, lens: list, cfg: ModelConfig, seed: int = 0):
         beta = torch.rand(1, T, Hv, generator=g, device=dev).bfloat16()
         ws = torch.empty(ops.delta_rule_workspace_bytes(T, len(lens), Hv), dtype=torch.uint8, device=dev)
         fn = lambda: ops.chunk_gated_delta_rule(q, k, v, gg, beta, cu_seqlens=cu, workspace=ws)  # noqa: E731
+        return fn, ("tensor", Hv * float(np.ceil(L / 64).sum()) * 11.7e6)
+    if op == "gdn_fused":  # conv + gates + delta rule from the in-projection, as the engine runs them
+        width = C + vd + 2 * Hv
+        proj = rn(T, width + (-width) % 8)
+        conv = rn(C, cfg.linear_conv_kernel_dim, scale=0.3)
+        A_log = torch.log(torch.empty(Hv, device=dev).uniform_(1, 16))
+        dt = torch.ones(Hv, device=dev)
+        ws = torch.empty(ops.delta_rule_workspace_bytes(T, len(lens), Hv), dtype=torch.uint8, device=dev)
+        fn = lambda: ops.gdn_fused_delta_rule(proj, conv, A_log, dt, Hv, C + vd + Hv, C + vd, cu, workspace=ws)  # noqa: E731
         return fn, ("tensor", Hv * float(np.ceil(L / 64).sum()) * 11.7e6)
     if op == "gqa_attention":
         q, k, v = rn(T, hq, D), rn(T, hkv, D), rn(T, hkv, D)

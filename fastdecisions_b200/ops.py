@@ -303,6 +303,41 @@ def chunk_gated_delta_rule(query, key, value, g, beta, chunk_size=64, initial_st
     return out, final
 
 
+def gdn_fused_delta_rule(proj: torch.Tensor, conv_weight: torch.Tensor, A_log: torch.Tensor, dt_bias: torch.Tensor,
+                         heads: int, a_col: int, b_col: int, cu_seqlens: torch.Tensor,
+                         workspace: Optional[torch.Tensor] = None, head_dim: int = 128) -> torch.Tensor:
+    """The Gated-DeltaNet mixer core straight from the in-projection ``proj [T, >= C]`` (bf16, unit
+    column stride): conv + SiLU of its q / k / v columns, the gates from columns ``a_col + h`` /
+    ``b_col + h``, and the chunked delta rule over the packed segments of ``cu_seqlens`` -- the
+    results of ``packed_conv_qkv``, ``gdn_gates`` and ``chunk_gated_delta_rule`` in one call.
+    Returns ``o [T, heads, 128]`` bf16."""
+    _need_cuda(proj, conv_weight, A_log, dt_bias, cu_seqlens)
+    if proj.dim() != 2 or proj.dtype != BF16 or proj.stride(1) != 1:
+        raise ValueError("gdn_fused_delta_rule: proj must be a bf16 [T, C] tensor with unit column stride")
+    if head_dim != 128:
+        raise ValueError("gdn_fused_delta_rule: head_dim must be 128")
+    T = proj.shape[0]
+    kd = vd = heads * head_dim
+    w = conv_weight.reshape(conv_weight.shape[0], conv_weight.shape[-1])
+    if w.dtype != BF16 or not w.is_contiguous() or w.shape != (2 * kd + vd, 4):
+        raise ValueError("gdn_fused_delta_rule: conv weight must be a contiguous bf16 [C, 4] (or [C, 1, 4]) tensor")
+    cu = cu_seqlens.to(torch.int32).contiguous()
+    nseg = cu.numel() - 1
+    ld = proj.stride(0) if T > 1 else proj.shape[1]
+    out = torch.empty((T, heads, head_dim), device=proj.device, dtype=BF16)
+    need = delta_rule_workspace_bytes(T, nseg, heads)
+    if workspace is None or workspace.numel() < need or workspace.data_ptr() % 256:
+        workspace = torch.empty(need, device=proj.device, dtype=torch.uint8)
+    al = A_log.float().contiguous()
+    dt = dt_bias.float().contiguous()
+    with torch.cuda.device(proj.device):
+        _lib.call("fdk_gdn_fused_delta_rule_fwd", proj.data_ptr(), ld, w.data_ptr(), 4, kd, vd, a_col, b_col,
+                  al.data_ptr(), dt.data_ptr(), cu.data_ptr(), nseg,
+                  T, heads, float(head_dim ** -0.5), None, out.data_ptr(), None, workspace.data_ptr(),
+                  workspace.numel(), _stream(proj))
+    return out
+
+
 # ------------------------------------------------------------------------------------------------
 # GDN gated norm, attention prologue, GQA attention, embedding, SwiGLU, readout
 # ------------------------------------------------------------------------------------------------

@@ -120,6 +120,30 @@ int fdk_chunk_gated_delta_rule_fwd(const void* q, const void* k, int64_t ld_qk, 
                                    void* stream);
 
 /*
+ * The Gated-DeltaNet mixer core from the projection: packed causal conv (width 4) + SiLU of the
+ * projection's q / k / v columns, the gates g = -exp(A_log) softplus(a + dt_bias) and
+ * beta = sigmoid(b) from its a / b columns, and the chunked delta rule -- one call, without the
+ * [T, H, 128] q / k / v and [T, H] g / beta round trips through HBM.
+ * Replaces the sequence the reference's linear-attention forward runs on the projection
+ * ([tf]:468-496 of transformers' modeling_qwen3_5.py: causal_conv1d_fn, the gate transform of
+ * src/decider/unpack_gate_transform_kernel.py:52-89, chunk_gated_delta_rule); its results are
+ * those of fdk_packed_conv_silu, fdk_gdn_gates and fdk_chunk_gated_delta_rule_fwd in sequence
+ * (same arithmetic and bf16 roundings).
+ *   proj        [tokens, ld_proj] bf16: columns [0, key_dim) q, [key_dim, 2 key_dim) k,
+ *               [2 key_dim, 2 key_dim + value_dim) v, a_col + h and b_col + h the gates' a and b
+ *   conv_weight [2 key_dim + value_dim, kernel_width] bf16 (kernel_width 4)
+ *   A_log, dt_bias [heads] fp32; key_dim = value_dim = heads x 128
+ *   workspace   as fdk_chunk_gated_delta_rule_fwd (same size function)
+ */
+int fdk_gdn_fused_delta_rule_fwd(const void* proj, int64_t ld_proj, const void* conv_weight,
+                                 int kernel_width, int64_t key_dim, int64_t value_dim,
+                                 int64_t a_col, int64_t b_col, const float* A_log,
+                                 const float* dt_bias, const int32_t* cu_seqlens,
+                                 int64_t num_segments, int64_t tokens, int64_t heads, float scale,
+                                 const float* initial_state, void* out, float* final_state,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Allocation-free form of fdk_chunk_gated_delta_rule_fwd (same arguments and results, no
  * workspace).  No counterpart in the reference.  It is for callers that cannot allocate device
  * memory: programs that reach this library only through its C ABI and own no device allocator

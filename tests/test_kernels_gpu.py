@@ -13,7 +13,7 @@ from oracle import ops as O
 pytestmark = pytest.mark.gpu
 
 if torch.cuda.is_available():
-    from fastdecisions_b200 import ops
+    from fastdecisions_b200 import _lib, ops
 
 MAX_ABS = 2e-2
 
@@ -305,3 +305,42 @@ def test_delta_rule_config4_layer_shape():
     # one GDN layer of config 4: T = 1536, 16 heads x 128
     err = delta_check(1536, 16, 7)
     assert err < MAX_ABS
+
+
+# --------------------------------------------------------------------------- fused GDN prologue
+def gdn_proj_inputs(lens, H, seed):
+    g = gen(seed)
+    T = sum(lens)
+    kd = vd = H * 128
+    C = 2 * kd + vd
+    width = C + vd + 2 * H
+    proj = torch.randn(T, width + (-width) % 8 + 8, generator=g).bfloat16()   # q k v | z | b | a | pad (16 B rows)
+    conv = (0.5 * torch.randn(C, 4, generator=g)).bfloat16()
+    A_log = torch.log(torch.empty(H).uniform_(1, 16, generator=g))
+    dt = 1.0 + 0.3 * torch.randn(H, generator=g)
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32)
+    return proj, conv, A_log, dt, cu, C, vd
+
+
+@pytest.mark.parametrize("lens", [[200], [1, 2, 3, 64, 65, 130, 7], [1536]])
+def test_gdn_fused_matches_separate_ops(lens):
+    H = 4
+    proj, conv, A_log, dt, cu, C, vd = gdn_proj_inputs(lens, H, 21)
+    P, W, AL, DT, CU = dev(proj), dev(conv), dev(A_log), dev(dt), dev(cu)
+    fused = ops.gdn_fused_delta_rule(P, W, AL, DT, H, C + vd + H, C + vd, CU)
+    q, k, v = ops.packed_conv_qkv(P[:, :C].unsqueeze(0), W, H * 128, vd, 128, CU)
+    gg, beta = ops.gdn_gates(P[:, C + vd + H:C + vd + 2 * H], P[:, C + vd:C + vd + H], AL, DT)
+    sep, _ = ops.chunk_gated_delta_rule(q, k, v, gg.unsqueeze(0), beta.unsqueeze(0), cu_seqlens=CU)
+    assert (fused.float() - sep[0].float()).abs().max().item() <= 1e-6
+    assert _lib.poll_device_error() == 0
+
+
+def test_gdn_fused_against_oracle():
+    H, lens = 2, [100, 1, 70]
+    proj, conv, A_log, dt, cu, C, vd = gdn_proj_inputs(lens, H, 22)
+    fused = ops.gdn_fused_delta_rule(dev(proj), dev(conv), dev(A_log), dev(dt), H, C + vd + H, C + vd, dev(cu))
+    q, k, v = O.packed_conv_silu(proj[:, :C].unsqueeze(0), conv, cu_seqlens=cu, key_dim=H * 128, value_dim=vd)
+    gg, beta = O.gdn_gates(proj[:, C + vd + H:C + vd + 2 * H].float(), proj[:, C + vd:C + vd + H].float(), A_log, dt)
+    ro, _ = O.chunk_gated_delta_rule(q.bfloat16().float(), k.bfloat16().float(), v.bfloat16().float(),
+                                     gg.unsqueeze(0), beta.bfloat16().float().unsqueeze(0), cu_seqlens=cu)
+    assert max_abs(fused.unsqueeze(0), ro) < MAX_ABS
