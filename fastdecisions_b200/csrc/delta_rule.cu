@@ -221,22 +221,16 @@ struct PrepIn {
   int64_t tokens;
 };
 
-// conv + SiLU of one 8-channel group over `rows` consecutive tokens starting at t, written as bf16
-// into a 128-byte-swizzled row of A1 (row base srow0, 16-byte chunk c16).  Rows before the segment
-// start read as zero (causal history restarts per segment); rows at or past `tokens` are zero.
+// conv + SiLU of one 8-channel group for ROWS consecutive tokens, from a raw projection box in
+// shared memory ([67 rows][64 channels] bf16, row r = token t0 - 3 + r, rows past the tokens
+// zero-filled by TMA), written as bf16 into a 128-byte-swizzled row of A1 (row srow0 + i, 16-byte
+// chunk c16).  Raw rows below `first_valid` precede the segment start and read as zero.
 template <int ROWS>
-__device__ __forceinline__ void conv_rows(const PrepIn& in, int64_t col, int64_t t, int64_t seg_start, uint8_t* a1,
-                                          int srow0, int c16) {
-  uint4 x[ROWS + 3];
-#pragma unroll
-  for (int i = 0; i < ROWS + 3; ++i) {
-    const int64_t tt = t - 3 + i;
-    x[i] = (tt >= seg_start && tt < in.tokens) ? __ldg(reinterpret_cast<const uint4*>(in.proj + tt * in.ld + col))
-                                               : make_uint4(0u, 0u, 0u, 0u);
-  }
+__device__ __forceinline__ void conv_rows(const uint8_t* box, int row0, int chunk, int first_valid, const bf16* wcol,
+                                          uint8_t* a1, int srow0, int c16) {
   float w[4][8];
   {
-    const uint4* wp = reinterpret_cast<const uint4*>(in.conv_w + col * 4);  // 8 channels x 4 taps, contiguous
+    const uint4* wp = reinterpret_cast<const uint4*>(wcol);  // 8 channels x 4 taps, contiguous
     float f[8];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -245,14 +239,21 @@ __device__ __forceinline__ void conv_rows(const PrepIn& in, int64_t col, int64_t
       for (int e = 0; e < 8; ++e) w[e & 3][2 * q + (e >> 2)] = f[e];
     }
   }
+  auto ld_row = [&](int r, float (&f)[8]) {
+    if (r >= first_valid) unpack8(*reinterpret_cast<const uint4*>(box + r * 128 + chunk * 16), f);
+    else {
+#pragma unroll
+      for (int c = 0; c < 8; ++c) f[c] = 0.f;
+    }
+  };
   float h0[8], h1[8], h2[8];
-  unpack8(x[0], h0);
-  unpack8(x[1], h1);
-  unpack8(x[2], h2);
+  ld_row(row0, h0);
+  ld_row(row0 + 1, h1);
+  ld_row(row0 + 2, h2);
 #pragma unroll
   for (int i = 0; i < ROWS; ++i) {
     float cur[8], y[8];
-    unpack8(x[i + 3], cur);
+    ld_row(row0 + 3 + i, cur);
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       float acc = w[3][c] * cur[c];
@@ -270,6 +271,7 @@ __device__ __forceinline__ void conv_rows(const PrepIn& in, int64_t col, int64_t
     }
   }
 }
+constexpr uint32_t RAW_BOX = 67 * 128;  // one raw projection box: 67 rows x 64 bf16
 
 template <bool CONV>
 __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
@@ -311,7 +313,18 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
   bool issued_v = false, issued_mma = false;
 
   // 1. raw k rows -> A1 rows 0-63, raw q rows -> rows 64-127 (TMA, 128-byte swizzle; rows past
-  //    the end of the tokens read as zero, rows of the next segment are masked below)
+  //    the end of the tokens read as zero, rows of the next segment are masked below).
+  //    CONV: the projection's raw k and q columns of this head, 3 history rows included, land in
+  //    the L / T area (free until the solve) as four [67][64] boxes: k0 k1 q0 q1.
+  if (CONV && tid == 0) {
+    prefetch_tmap(&mq);
+    mbar_expect_tx(bar0 + 8 * B_QK, 4 * RAW_BOX);
+#pragma unroll
+    for (int bx = 0; bx < 4; ++bx) {
+      const int col = (bx < 2 ? in.key_dim : 0) + h * DR_D + (bx & 1) * 64;
+      tma_load_2d(base + LF + bx * RAW_BOX, &mq, bar0 + 8 * B_QK, col, t0 - 3);
+    }
+  }
   if (!CONV && tid == 0) {
     prefetch_tmap(&mq);
     prefetch_tmap(&mk);
@@ -359,15 +372,24 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
     fw[r1] = b1 * expf(G1);
     if (lane == 31) *reinterpret_cast<float*>(tile + OFF_GAMMA) = expf(G1);
   }
-  if (CONV) {  // q (A1 rows 64-127) and k (rows 0-63): thread = 8 channels x 8 tokens, in two runs of 4
+  bool ok = mbar_wait(bar0 + 8 * B_QK, 0, abort_flag);
+  if (CONV && ok) {  // q (A1 rows 64-127) and k (rows 0-63): thread = 8 channels x 8 tokens
     const int g8 = tid & 31, rs = tid >> 5;
     const bool isk = g8 >= 16;
-    const int64_t col = (isk ? in.key_dim : 0) + (int64_t)h * DR_D + (g8 & 15) * 8;
-    conv_rows<4>(in, col, (int64_t)t0 + rs * 8, seg_start, sb + A1, (isk ? 0 : 64) + rs * 8, g8 & 15);
-    conv_rows<4>(in, col, (int64_t)t0 + rs * 8 + 4, seg_start, sb + A1, (isk ? 0 : 64) + rs * 8 + 4, g8 & 15);
+    const int c16 = g8 & 15;
+    const int first_valid = max(0, seg_start - (t0 - 3));
+    const bf16* wcol = in.conv_w + ((isk ? in.key_dim : 0) + (int64_t)h * DR_D + c16 * 8) * 4;
+    const uint8_t* box = sb + LF + ((isk ? 0 : 2) + (c16 >> 3)) * RAW_BOX;
+    conv_rows<8>(box, rs * 8, c16 & 7, first_valid, wcol, sb + A1, (isk ? 0 : 64) + rs * 8, c16);
+    fence_proxy_async_smem();  // the raw boxes are refilled by TMA (V) below
   }
-  bool ok = CONV ? true : mbar_wait(bar0 + 8 * B_QK, 0, abort_flag);
   ok = __syncthreads_and(ok) != 0;  // also publishes G2 / beta / fw
+  if (CONV && ok && tid == 0) {  // raw v columns -> the T area, landing while k / q are normalised
+    mbar_expect_tx(bar0 + 8 * B_V, 2 * RAW_BOX);
+    tma_load_2d(base + TF, &mq, bar0 + 8 * B_V, 2 * in.key_dim + h * DR_D, t0 - 3);
+    tma_load_2d(base + TF + RAW_BOX, &mq, bar0 + 8 * B_V, 2 * in.key_dim + h * DR_D + 64, t0 - 3);
+    issued_v = true;
+  }
 
   if (ok) {
     // 2. l2-normalise k and q rows (q also times scale) in place, zero rows past the length;
@@ -427,10 +449,12 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
   if (ok) ok = warp_wait(bar0 + 8 * B_MMA1, 0, abort_flag);
   if (ok) tc_fence_after();
   // V rows -> A1 rows 64-127 (q^ is no longer read), landing while the solve runs
-  if (CONV && ok) {  // v by conv: thread = 8 channels x 4 tokens
+  if (CONV && ok) ok = warp_wait(bar0 + 8 * B_V, 0, abort_flag);
+  if (CONV && ok) {  // v by conv into A1 rows 64-127: thread = 8 channels x 4 tokens
     const int g8 = tid & 15, rs = tid >> 4;
-    conv_rows<4>(in, 2 * (int64_t)in.key_dim + (int64_t)h * DR_D + g8 * 8, (int64_t)t0 + rs * 4, seg_start, sb + A1,
-                 64 + rs * 4, g8);
+    const int first_valid = max(0, seg_start - (t0 - 3));
+    const bf16* wcol = in.conv_w + (2 * (int64_t)in.key_dim + (int64_t)h * DR_D + g8 * 8) * 4;
+    conv_rows<4>(sb + TF + (g8 >> 3) * RAW_BOX, rs * 4, g8 & 7, first_valid, wcol, sb + A1, 64 + rs * 4, g8);
     fence_proxy_async_smem();
   }
   if (!CONV && ok && tid == 0) {
@@ -608,7 +632,7 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
   // shared memory are released
   if (tid == 0 && *abort_flag) {
     volatile int never = 0;
-    if (!CONV) mbar_wait(bar0 + 8 * B_QK, 0, &never, DRAIN_BUDGET);
+    mbar_wait(bar0 + 8 * B_QK, 0, &never, DRAIN_BUDGET);
     if (issued_v) mbar_wait(bar0 + 8 * B_V, 0, &never, DRAIN_BUDGET);
     if (issued_mma) {  // every MMA this thread issued has completed
       umma_commit(bar0 + 8 * B_DRAIN);
@@ -1009,6 +1033,23 @@ static int act_map(CUtensorMap* m, const void* ptr, int64_t tokens, int64_t head
   return FDK_OK;
 }
 
+// 2-D map over the first `cols` columns of a [tokens, ld] bf16 projection, box 64 x 67 (one
+// 64-token chunk plus 3 history rows), no swizzle: the fused prologue's raw conv input.
+static int raw_map(CUtensorMap* m, const void* ptr, int64_t tokens, int64_t cols, int64_t ld) {
+  EncodeFn enc = encode_fn();
+  if (!enc) return set_error(FDK_ERR_DEVICE, "gdn_fused_delta_rule: cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)tokens};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {64, 67};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(FDK_ERR_INVALID_ARGUMENT, "gdn_fused_delta_rule: tensor map encode failed (%d)", (int)r);
+  return FDK_OK;
+}
+
 }  // namespace drtc
 
 int delta_take_device_error() {
@@ -1081,10 +1122,10 @@ static int run_delta_rule(bool conv, const void* q, const void* k, int64_t ld_qk
   if (tokens == 0 && !final_state) return FDK_OK;
   if (tokens > 0) {
     CUtensorMap mq, mk, mv;
-    if (conv) {  // the conv prologue reads the projection directly; the maps are never used
-      memset(&mq, 0, sizeof(mq));
+    if (conv) {  // the fused prologue reads the projection through one map (passed as mq)
       memset(&mk, 0, sizeof(mk));
       memset(&mv, 0, sizeof(mv));
+      if (int st = drtc::raw_map(&mq, in.proj, tokens, 3 * (int64_t)in.key_dim, in.ld)) return st;
     } else {
       if (int st = drtc::act_map(&mq, q, tokens, heads, ld_qk)) return st;
       if (int st = drtc::act_map(&mk, k, tokens, heads, ld_qk)) return st;
