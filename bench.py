@@ -36,6 +36,17 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 REQUESTS_PER_GPU = 256  # config 5; --requests-per-gpu changes it only for small profiling runs
+
+# DRAM bytes (read + write) per token of one launch, from one ncu capture of each op on config-5
+# batch 7 (32767 tokens; profiles/*.md give the commands); a launch's traffic is this times its
+# tokens (all these ops move bytes in proportion to the tokens they process).
+NCU_DRAM_BYTES_PER_TOKEN = {
+    "delta_rule": (475.78e6 + 575.00e6 + 625.47e6 + 118.14e6) / 32767,  # fused prep + recurrence
+    "gqa_attention": (282.43e6 + 96.97e6) / 32767,
+    "packed_conv": (403.93e6 + 351.90e6) / 32767,
+    "qk_norm_rope": (168.06e6 + 124.66e6) / 32767,
+    "residual_rmsnorm": (402.88e6 + 345.73e6) / 32767,
+}
 METRIC = ("requests/sec, config 5 (256 seeded requests per GPU, lognormal lengths median 800 in [64, 8192], "
           "2-8 options) through the config-4 2B-class hybrid decision forward")
 PEAKS_FALLBACK = dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0)
@@ -400,7 +411,9 @@ def run_ours(args, world, rank, local):
             achieved, peak, unit = units * args.steps / secs / 1e9, pk["hbm_gbs"], "GB/s"
             src = f"{pk_kind} hbm_gbs"
         roof[name] = {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
-                      "traffic": None, "kernel": name, "launches": tot[name]["launches"],
+                      "traffic": (NCU_DRAM_BYTES_PER_TOKEN[name] * sum(b.tokens for b in batches) /
+                                  len(batches)) if name in NCU_DRAM_BYTES_PER_TOKEN else None,
+                      "kernel": name, "launches": tot[name]["launches"],
                       "total_ms": tot[name]["total_ms"], "share_of_step": tot[name]["total_ms"] / step_ms_local,
                       "per_launch_units": units / max(1, tot[name]["launches"] // args.steps), "peak_source": src}
     own = {k: v for k, v in roof.items() if k != "gemm"}
