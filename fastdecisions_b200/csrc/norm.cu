@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(256) gated_rmsnorm_kernel(
 
 // ---------------------------------------------------------------------------------------------
 // q/k RMSNorm (1 + w) over head_dim + partial rotary embedding.  One warp per token: it walks the
-// token's hq + hkv head rows, four at a time with all four rows' loads issued first.  Lane l holds
+// token's hq + hkv head rows, ten at a time with all ten rows' loads issued first.  Lane l holds
 // features [l*E, l*E + E) of every row (E = head_dim / 32: 4 for 128, 8 for 256), so its norm
 // weights, cos / sin factors and rotate_half partner lane are loaded and computed once per token.
 // rotate_half pairs feature i with i + rot/2 inside the first rot features.
@@ -186,7 +186,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
     const int32_t* __restrict__ pos, const float* __restrict__ rope, int max_pos, int rot, bf16* __restrict__ qo,
     bf16* __restrict__ ko, int64_t tokens, int hq, int hkv, float eps) {
   constexpr int D = E * 32;
-  constexpr int G = 4;  // rows in flight per warp
+  constexpr int G = 10;  // rows in flight per warp (hq + hkv = 20 for the decision model: two rounds)
   const int64_t t = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= tokens) return;
