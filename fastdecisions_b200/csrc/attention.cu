@@ -24,7 +24,6 @@
 #include <math.h>
 
 #include "common.cuh"
-#include "mma_sm80.cuh"
 #include "sm100.cuh"
 
 namespace fdk {

@@ -21,7 +21,6 @@
 #include <string.h>
 
 #include "common.cuh"
-#include "mma_sm80.cuh"
 #include "sm100.cuh"
 
 namespace fdk {

@@ -4,6 +4,12 @@
 #include <stdint.h>
 
 namespace fdk {
+
+// shared-memory address of a generic pointer into shared memory
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
 namespace sm100 {
 
 // ----------------------------------------------------------------------------- mbarrier
