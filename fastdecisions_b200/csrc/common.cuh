@@ -76,9 +76,6 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// silu(x) = x * sigmoid(x) with the hardware exp2 and approximate reciprocal (2 MUFU ops).
-// x -> +inf gives x, x -> -inf gives -0 (the reciprocal of +inf is 0).
-__device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 // silu(x) = 0.5 x (1 + tanh(x / 2)) with the hardware tanh (tanh.approx.f32, relative error about
 // 2^-11): one MUFU op instead of two, for kernels whose MUFU pipe is the limit.  Its error is well
 // below the bf16 rounding of the results these kernels store.
