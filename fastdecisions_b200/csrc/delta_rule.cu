@@ -2,15 +2,16 @@
 //
 // Restates transformers' torch_chunk_gated_delta_rule (models/qwen3_5/modeling_qwen3_5.py:234-311)
 // for packed varlen input.  Three launches (four with final states):
-//   1. chunk_table_kernel : per-segment chunk offsets and per-chunk (first token, length), device
-//      side and graph-capturable.
+//   1. chunk_table_kernel : per-segment chunk offsets and per-chunk (first token, length, segment
+//      start), device side and graph-capturable.
 //   2. delta_prep_kernel  : one 256-thread CTA per (chunk, head), fully parallel, three CTAs per
-//      SM.  TMA brings the raw q / k rows, the CTA l2-normalises them, takes the in-chunk cumsum G
-//      of the log decay, forms [K;Q] K^T as one M=128 tcgen05 MMA, inverts the unit-lower-
-//      triangular (I - L) from 16x16 block products (diagonal blocks by repeated squaring, then
-//      block forward substitution; mma.sync tf32 with the 3xTF32 split, fp32-accurate), and
-//      forms U^T and W^T as two more tcgen05 MMAs (V and K as MN-major A operands).  It writes
-//      into the caller's workspace (bf16)
+//      SM.  TMA brings the raw q / k rows (or, fused, the raw projection columns, which the CTA
+//      convolves itself, computing the gates from the projection too), the CTA l2-normalises
+//      them, takes the in-chunk cumsum G of the log decay, forms [K;Q] K^T as one M=128 tcgen05
+//      MMA, inverts the unit-lower-triangular (I - L) in fp32 (diagonal 16x16 blocks by row
+//      substitution in registers, then off-diagonal blocks by 16x16 block products on mma.sync
+//      tf32 with the 3xTF32 split), and forms U^T and W^T as two more tcgen05 MMAs (V and K as
+//      MN-major A operands).  It writes into the caller's workspace (bf16)
 //        W^T = (T diag(beta e^G) K)^T   U^T = (T diag(beta) V)^T     Aqk = (QK^T o decay), lower
 //        Qg  = q e^G                    Kg  = k e^(G_last - G)       gamma = e^G_last (fp32)
 //   3. delta_recur_tc_kernel : persistent; each CTA takes (segment, head) chains from a work
