@@ -55,21 +55,49 @@ template <bool W_FP32, bool HID_FP32>
 __global__ void __launch_bounds__(256) slot_readout_kernel(
     const void* __restrict__ hidden, const bf16* __restrict__ delta, int hsz, const int32_t* __restrict__ slots,
     const int32_t* __restrict__ nopts, const void* __restrict__ fw, const bf16* __restrict__ letters, int K,
-    float eps, float temp, float* __restrict__ probs, float* __restrict__ logits) {
+    float eps, float temp, float* __restrict__ probs, float* __restrict__ logits, int vec) {
   const int n = blockIdx.x;
   const int64_t r = (int64_t)slots[n] * hsz;
   __shared__ float rowv[READOUT_MAX_H];   // the slot row after the final residual add (bf16 values)
   __shared__ float red[8][17];
   __shared__ float s_inv;
   float ss = 0.f;
-  for (int i = threadIdx.x; i < hsz; i += 256) {
-    float x = HID_FP32 ? static_cast<const float*>(hidden)[r + i] : __bfloat162float(static_cast<const bf16*>(hidden)[r + i]);
-    if (delta) {
-      x += __bfloat162float(delta[r + i]);
-      if (!HID_FP32) x = round_bf16(x);  // the bf16 residual stream rounds the last add
+  if (vec) {
+    // 16-byte aligned rows with hsz % 8 == 0 (the decision model): 8 elements per thread and pass,
+    // all of a pass's loads in flight at once (one block per slot: latency, not bandwidth)
+    for (int i = threadIdx.x * 8; i < hsz; i += 256 * 8) {
+      float x[8], d[8];
+      if (HID_FP32) {
+        const float4* hp = reinterpret_cast<const float4*>(static_cast<const float*>(hidden) + r + i);
+        const float4 a = hp[0], b = hp[1];
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+      } else {
+        unpack8(*reinterpret_cast<const uint4*>(static_cast<const bf16*>(hidden) + r + i), x);
+      }
+      if (delta) {
+        unpack8(*reinterpret_cast<const uint4*>(delta + r + i), d);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          x[e] += d[e];
+          if (!HID_FP32) x[e] = round_bf16(x[e]);  // the bf16 residual stream rounds the last add
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        rowv[i + e] = x[e];
+        ss = fmaf(x[e], x[e], ss);
+      }
     }
-    rowv[i] = x;
-    ss = fmaf(x, x, ss);
+  } else {
+    for (int i = threadIdx.x; i < hsz; i += 256) {
+      float x = HID_FP32 ? static_cast<const float*>(hidden)[r + i] : __bfloat162float(static_cast<const bf16*>(hidden)[r + i]);
+      if (delta) {
+        x += __bfloat162float(delta[r + i]);
+        if (!HID_FP32) x = round_bf16(x);
+      }
+      rowv[i] = x;
+      ss = fmaf(x, x, ss);
+    }
   }
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5][16] = ss;
@@ -84,12 +112,34 @@ __global__ void __launch_bounds__(256) slot_readout_kernel(
   float acc[16];
 #pragma unroll
   for (int k = 0; k < 16; ++k) acc[k] = 0.f;
-  for (int i = threadIdx.x; i < hsz; i += 256) {
-    const float wf = W_FP32 ? static_cast<const float*>(fw)[i] : __bfloat162float(static_cast<const bf16*>(fw)[i]);
-    const float hn = rowv[i] * inv * (1.0f + wf);
+  if (vec && !W_FP32) {  // (vec also guarantees 16-byte aligned weight and letter rows)
+    for (int i = threadIdx.x * 8; i < hsz; i += 256 * 8) {
+      float wf[8], hn[8];
+      unpack8(*reinterpret_cast<const uint4*>(static_cast<const bf16*>(fw) + i), wf);
 #pragma unroll
-    for (int k = 0; k < 16; ++k)
-      if (k < K) acc[k] = fmaf(hn, __bfloat162float(letters[(int64_t)k * hsz + i]), acc[k]);
+      for (int e = 0; e < 8; ++e) hn[e] = rowv[i + e] * inv * (1.0f + wf[e]);
+      uint4 lw[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+        if (k < K) lw[k] = *reinterpret_cast<const uint4*>(letters + (int64_t)k * hsz + i);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        if (k < K) {
+          float l[8];
+          unpack8(lw[k], l);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[k] = fmaf(hn[e], l[e], acc[k]);
+        }
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < hsz; i += 256) {
+      const float wf = W_FP32 ? static_cast<const float*>(fw)[i] : __bfloat162float(static_cast<const bf16*>(fw)[i]);
+      const float hn = rowv[i] * inv * (1.0f + wf);
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+        if (k < K) acc[k] = fmaf(hn, __bfloat162float(letters[(int64_t)k * hsz + i]), acc[k]);
+    }
   }
   __syncthreads();
 #pragma unroll
@@ -174,12 +224,14 @@ extern "C" int fdk_slot_readout(const void* hidden, int hidden_is_fp32, const vo
   auto lb = static_cast<const bf16*>(letters);
   const unsigned g = (unsigned)num_slots;
   const int H = (int)hidden_size, K = (int)num_letters;
+  const int vec = (H % 8 == 0) && aligned16(hidden) && (!delta || aligned16(delta)) && aligned16(final_norm_w) &&
+                  aligned16(letters);
   if (weight_is_fp32) {
-    if (hidden_is_fp32) slot_readout_kernel<true, true><<<g, 256, 0, s>>>(hidden, db, H, slots, nopts, final_norm_w, lb, K, eps, temperature, probs, logits);
-    else slot_readout_kernel<true, false><<<g, 256, 0, s>>>(hidden, db, H, slots, nopts, final_norm_w, lb, K, eps, temperature, probs, logits);
+    if (hidden_is_fp32) slot_readout_kernel<true, true><<<g, 256, 0, s>>>(hidden, db, H, slots, nopts, final_norm_w, lb, K, eps, temperature, probs, logits, vec);
+    else slot_readout_kernel<true, false><<<g, 256, 0, s>>>(hidden, db, H, slots, nopts, final_norm_w, lb, K, eps, temperature, probs, logits, vec);
   } else {
-    if (hidden_is_fp32) slot_readout_kernel<false, true><<<g, 256, 0, s>>>(hidden, db, H, slots, nopts, final_norm_w, lb, K, eps, temperature, probs, logits);
-    else slot_readout_kernel<false, false><<<g, 256, 0, s>>>(hidden, db, H, slots, nopts, final_norm_w, lb, K, eps, temperature, probs, logits);
+    if (hidden_is_fp32) slot_readout_kernel<false, true><<<g, 256, 0, s>>>(hidden, db, H, slots, nopts, final_norm_w, lb, K, eps, temperature, probs, logits, vec);
+    else slot_readout_kernel<false, false><<<g, 256, 0, s>>>(hidden, db, H, slots, nopts, final_norm_w, lb, K, eps, temperature, probs, logits, vec);
   }
   return check_launch("slot_readout");
 }
