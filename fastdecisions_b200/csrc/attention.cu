@@ -4,13 +4,15 @@
 // every K/V tile brought into shared memory feeds two heads.  Warp roles (320 threads):
 //   warps 0-3  softmax of head A (thread = query row = TMEM lane)
 //   warps 4-7  softmax of head B
-//   warp  8    TMA producer: Q (once), K ring of 2 stages, V single stage
+//   warp  8    TMA producer: Q (once), K and V rings of 2 stages each
 //   warp  9    TMEM allocator + single-thread tcgen05.mma issuer
 // TMEM (512 columns): S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512), fp32.
 // The issuer runs S_A = Q_A K_0^T and S_B = Q_B K_0^T, then per KV block j: O_A += P_A V_j once
-// the head-A softmax has written P_A (bf16, 128B-swizzled K-major tile in shared memory),
-// S_A = Q_A K_{j+1}^T, O_B += P_B V_j, S_B = Q_B K_{j+1}^T.  Head A's softmax of block j+1 thus
-// overlaps head B's of block j, and the tensor core always has the other head's work queued.
+// the head-A softmax has written P_A (bf16 pairs over the first 64 columns of S_A: the PV MMA
+// takes A from TMEM), S_A = Q_A K_{j+1}^T, O_B += P_B V_j, S_B = Q_B K_{j+1}^T.  Head A's
+// softmax of block j+1 thus overlaps head B's of block j, and the tensor core always has the
+// other head's work queued; MMAs of one thread execute in issue order, so S_A(j+1) overwrites
+// P_A(j) only after the PV that reads it.
 // Softmax is online in fp32 in the exp2 domain with lazy rescaling of O (only when the running
 // max grows by more than 2^8).  The causal mask is applied only on the diagonal block; rows of a
 // tile past the end of its segment are computed but never stored.  Varlen: cu_seqlens gives
@@ -33,9 +35,9 @@ using namespace sm100;
 constexpr int BM = 128, BN = 128, HD = 128;
 constexpr uint32_t HALF = 128 * 128;  // 128 rows x 128 B (64 bf16): one swizzle-128B box
 constexpr uint32_t TILE = 2 * HALF;   // 128 x 128 bf16
-constexpr uint32_t OFF_QA = 0, OFF_QB = TILE, OFF_K0 = 2 * TILE, OFF_K1 = 3 * TILE, OFF_V = 4 * TILE,
-                   OFF_PA = 5 * TILE, OFF_PB = 6 * TILE, OFF_BAR = 7 * TILE;
-enum { B_Q = 0, B_KF0, B_KF1, B_KE0, B_KE1, B_VF, B_VE, B_SA, B_SB, B_PA, B_PB, B_O, NBAR };
+constexpr uint32_t OFF_QA = 0, OFF_QB = TILE, OFF_K0 = 2 * TILE, OFF_K1 = 3 * TILE, OFF_V0 = 4 * TILE,
+                   OFF_V1 = 5 * TILE, OFF_BAR = 6 * TILE;
+enum { B_Q = 0, B_KF0, B_KF1, B_KE0, B_KE1, B_VF0, B_VF1, B_VE0, B_VE1, B_SA, B_SB, B_PA, B_PB, B_O, NBAR };
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 8 * NBAR + 16 + 1024;  // + slack for 1024-B alignment
 constexpr int NUM_THREADS = 320;
 constexpr uint32_t TM_SA = 0, TM_SB = 128, TM_OA = 256, TM_OB = 384, TM_COLS = 512;
@@ -118,16 +120,17 @@ gqa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
         tma_load_2d(kdst, &tk, bar0 + 8 * (B_KF0 + ks), hk * HD, seg0 + j * BN);
         tma_load_2d(kdst + HALF, &tk, bar0 + 8 * (B_KF0 + ks), hk * HD + 64, seg0 + j * BN);
         issued_k = j + 1;
-        if (j >= 1 && !mbar_wait(bar0 + 8 * B_VE, (j - 1) & 1, abort_flag)) break;
-        mbar_expect_tx(bar0 + 8 * B_VF, TILE);
-        tma_load_2d(base + OFF_V, &tv, bar0 + 8 * B_VF, hk * HD, seg0 + j * BN);
-        tma_load_2d(base + OFF_V + HALF, &tv, bar0 + 8 * B_VF, hk * HD + 64, seg0 + j * BN);
+        if (j >= 2 && !mbar_wait(bar0 + 8 * (B_VE0 + ks), ((j >> 1) - 1) & 1, abort_flag)) break;
+        const uint32_t vdst = base + (ks ? OFF_V1 : OFF_V0);
+        mbar_expect_tx(bar0 + 8 * (B_VF0 + ks), TILE);
+        tma_load_2d(vdst, &tv, bar0 + 8 * (B_VF0 + ks), hk * HD, seg0 + j * BN);
+        tma_load_2d(vdst + HALF, &tv, bar0 + 8 * (B_VF0 + ks), hk * HD + 64, seg0 + j * BN);
         issued_v = j + 1;
       }
       // drain: every issued load must have landed before shared memory is released
       drain(bar0 + 8 * B_Q, 0);
       for (int j = (issued_k > 2 ? issued_k - 2 : 0); j < issued_k; ++j) drain(bar0 + 8 * (B_KF0 + (j & 1)), (j >> 1) & 1);
-      if (issued_v > 0) drain(bar0 + 8 * B_VF, (issued_v - 1) & 1);
+      for (int j = (issued_v > 2 ? issued_v - 2 : 0); j < issued_v; ++j) drain(bar0 + 8 * (B_VF0 + (j & 1)), (j >> 1) & 1);
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------------ MMA issuer
@@ -140,7 +143,7 @@ gqa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
       // same head issued before it (O rescale and P-tile reuse rely on that).
       // descriptors built once; a k step adds its byte offset / 16 to the start-address field
       // (shared-memory addresses stay below 2^18, so the field never carries)
-      const uint64_t dV = sdesc_sw128(base + OFF_V, HALF, 1024);
+
       auto issue_s = [&](int j, uint32_t q_off, uint32_t tm, uint32_t bar) {
         const uint64_t dq = sdesc_sw128(base + q_off, 16, 1024);
         const uint64_t dk = sdesc_sw128(base + ((j & 1) ? OFF_K1 : OFF_K0), 16, 1024);
@@ -151,13 +154,13 @@ gqa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
         }
         umma_commit(bar);
       };
-      auto issue_pv = [&](int j, uint32_t p_off, uint32_t tm) {
-        const uint64_t dp = sdesc_sw128(base + p_off, 16, 1024);
+      // O += P V with P (bf16, packed two per column) in the first 64 TMEM columns of the head's S
+      // region: the softmax overwrote S with P; the next S MMA of the head is issued after this one
+      auto issue_pv = [&](int j, uint32_t tm_p, uint32_t tm) {
+        const uint64_t dV = sdesc_sw128(base + ((j & 1) ? OFF_V1 : OFF_V0), HALF, 1024);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t aoff = ((kk >> 2) * HALF + (kk & 3) * 32) >> 4;
-          umma_ss(tmem + tm, dp + aoff, dV + (uint32_t)(kk * 2048 >> 4), ID_PV, (j > 0 || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < 8; ++kk)
+          umma_ts(tmem + tm, tmem + tm_p + 8 * kk, dV + (uint32_t)(kk * 2048 >> 4), ID_PV, (j > 0 || kk > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(bar0 + 8 * B_Q, 0, abort_flag) && mbar_wait(bar0 + 8 * B_KF0, 0, abort_flag);
       if (ok) {
@@ -168,10 +171,10 @@ gqa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
       }
       for (int j = 0; ok && j < n_kv; ++j) {
         const bool more = j + 1 < n_kv;
-        if (!mbar_wait(bar0 + 8 * B_VF, j & 1, abort_flag)) break;
+        if (!mbar_wait(bar0 + 8 * (B_VF0 + (j & 1)), (j >> 1) & 1, abort_flag)) break;
         if (!mbar_wait(bar0 + 8 * B_PA, j & 1, abort_flag)) break;
         tc_fence_after();
-        issue_pv(j, OFF_PA, TM_OA);
+        issue_pv(j, TM_SA, TM_OA);
         if (more) {
           if (!mbar_wait(bar0 + 8 * (B_KF0 + ((j + 1) & 1)), ((j + 1) >> 1) & 1, abort_flag)) break;
           tc_fence_after();
@@ -179,8 +182,8 @@ gqa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
         }
         if (!mbar_wait(bar0 + 8 * B_PB, j & 1, abort_flag)) break;
         tc_fence_after();
-        issue_pv(j, OFF_PB, TM_OB);
-        umma_commit(bar0 + 8 * B_VE);
+        issue_pv(j, TM_SB, TM_OB);
+        umma_commit(bar0 + 8 * (B_VE0 + (j & 1)));
         if (more) {
           issue_s(j + 1, OFF_QB, TM_SB, bar0 + 8 * B_SB);
           umma_commit(bar0 + 8 * (B_KE0 + ((j + 1) & 1)));
@@ -198,7 +201,6 @@ gqa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     const uint32_t tO = tmem + lane_base + (wg ? TM_OB : TM_OA);
     const uint32_t bS = bar0 + 8 * (wg ? B_SB : B_SA);
     const uint32_t bP = bar0 + 8 * (wg ? B_PB : B_PA);
-    uint8_t* P = gbase + (wg ? OFF_PB : OFF_PA);
     const float sl2 = p.sl2;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
@@ -237,23 +239,22 @@ gqa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
         m_run = m_new;
         rescale = true;
       }
-      // P = exp2(S * scale * log2e - m_run) as bf16 into the swizzled K-major tile; the row sum
-      // in 8 independent partial sums
+      // P = exp2(S * scale * log2e - m_run) as bf16 pairs over the first 64 columns of this row's
+      // S (the PV MMA reads A from TMEM); the row sum in 8 independent partial sums
       float sum8[8];
 #pragma unroll
       for (int a = 0; a < 8; ++a) sum8[a] = 0.f;
+      uint32_t pk[2][32];
 #pragma unroll
-      for (int c16 = 0; c16 < 16; ++c16) {
-        float e[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int col = c16 * 8 + i;
-          e[i] = ex2(fmaf(__uint_as_float(sr[col >> 5][col & 31]), sl2, -m_run));
-          sum8[i] += e[i];
-        }
-        const uint32_t off = (uint32_t)(c16 >> 3) * HALF + (uint32_t)row * 128u + ((uint32_t)((c16 & 7) ^ (row & 7)) << 4);
-        *reinterpret_cast<uint4*>(P + off) = pack8(e);
+      for (int c = 0; c < 64; ++c) {
+        const float e0 = ex2(fmaf(__uint_as_float(sr[(2 * c) >> 5][(2 * c) & 31]), sl2, -m_run));
+        const float e1 = ex2(fmaf(__uint_as_float(sr[(2 * c + 1) >> 5][(2 * c + 1) & 31]), sl2, -m_run));
+        sum8[(2 * c) & 7] += e0;
+        sum8[(2 * c + 1) & 7] += e1;
+        pk[c >> 5][c & 31] = pack_bf16x2(e0, e1);
       }
+      tmem_st32(tS, pk[0]);
+      tmem_st32(tS + 32, pk[1]);
       const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
       l_run = l_run * alpha + sum;
       if (rescale) {  // O row *= alpha (PV of block j-1 has completed: S_j's commit covers it)
@@ -266,9 +267,8 @@ gqa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
           for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
           tmem_st32(tO + c * 32, o);
         }
-        tmem_st_wait();
       }
-      fence_proxy_async_smem();
+      tmem_st_wait();
       tc_fence_before();
       mbar_arrive(bP);
     }
