@@ -195,7 +195,7 @@ constexpr uint32_t A1 = 0;                    // [2 dk halves][128 rows][128 B]:
 constexpr uint32_t LF = 32768;                // fp32 L [64][LDF]; after the solve TU and TW (8 KB each)
 constexpr uint32_t TU_OFF = LF, TW_OFF = LF + 8192;
 constexpr uint32_t TF = LF + 64 * LDF * 4;    // fp32 T [64][LDF]
-constexpr uint32_t VEC = TF + 64 * LDF * 4;   // G * log2(e), beta, beta, beta e^G: [4][64] fp32
+constexpr uint32_t VEC = TF + 64 * LDF * 4;   // G * log2(e), beta, beta e^G, -G * log2(e): [4][64] fp32
 constexpr uint32_t BARS = VEC + 4 * 64 * 4;
 enum { B_QK = 0, B_MMA1, B_V, B_MMA2, B_DRAIN, NBAR };
 constexpr uint32_t SMEM_BYTES = BARS + 8 * NBAR + 16 + 1024;
@@ -228,7 +228,9 @@ struct PrepIn {
 template <int ROWS>
 __device__ __forceinline__ void conv_rows(const uint8_t* box, int row0, int chunk, int first_valid, const bf16* wcol,
                                           uint8_t* a1, int srow0, int c16) {
-  float w[4][8];
+  // Channel pairs run on the packed fp32 pipe (fma.rn.f32x2): per lane the same roundings as
+  // the scalar mul / fma chain of the packed-conv kernel.
+  float2 w[4][4];
   {
     const uint4* wp = reinterpret_cast<const uint4*>(wcol);  // 8 channels x 4 taps, contiguous
     float f[8];
@@ -236,35 +238,45 @@ __device__ __forceinline__ void conv_rows(const uint8_t* box, int row0, int chun
     for (int q = 0; q < 4; ++q) {
       unpack8(__ldg(wp + q), f);  // channels 2q, 2q+1, taps 0..3 each
 #pragma unroll
-      for (int e = 0; e < 8; ++e) w[e & 3][2 * q + (e >> 2)] = f[e];
+      for (int t = 0; t < 4; ++t) w[t][q] = make_float2(f[t], f[4 + t]);
     }
   }
-  auto ld_row = [&](int r, float (&f)[8]) {
-    if (r >= first_valid) unpack8(*reinterpret_cast<const uint4*>(box + r * 128 + chunk * 16), f);
-    else {
+  auto ld_row = [&](int r, float2 (&f)[4]) {
+    if (r >= first_valid) {
+      const uint4 u = *reinterpret_cast<const uint4*>(box + r * 128 + chunk * 16);
+      f[0] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+      f[1] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+      f[2] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.z));
+      f[3] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.w));
+    } else {
 #pragma unroll
-      for (int c = 0; c < 8; ++c) f[c] = 0.f;
+      for (int c = 0; c < 4; ++c) f[c] = make_float2(0.f, 0.f);
     }
   };
-  float h0[8], h1[8], h2[8];
+  const float2 half2 = make_float2(0.5f, 0.5f);
+  float2 h0[4], h1[4], h2[4];
   ld_row(row0, h0);
   ld_row(row0 + 1, h1);
   ld_row(row0 + 2, h2);
 #pragma unroll
   for (int i = 0; i < ROWS; ++i) {
-    float cur[8], y[8];
+    float2 cur[4];
+    uint4 out;
+    uint32_t* o = reinterpret_cast<uint32_t*>(&out);
     ld_row(row0 + 3 + i, cur);
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      float acc = w[3][c] * cur[c];
-      acc = fmaf(w[2][c], h2[c], acc);
-      acc = fmaf(w[1][c], h1[c], acc);
-      acc = fmaf(w[0][c], h0[c], acc);
-      y[c] = silu_tanh(acc);
+    for (int c = 0; c < 4; ++c) {
+      float2 acc = __fmul2_rn(w[3][c], cur[c]);
+      acc = __ffma2_rn(w[2][c], h2[c], acc);
+      acc = __ffma2_rn(w[1][c], h1[c], acc);
+      acc = __ffma2_rn(w[0][c], h0[c], acc);
+      const float2 hh = __fmul2_rn(half2, acc);  // silu(x) = h + h tanh(h), h = x / 2
+      const float2 y = __ffma2_rn(hh, make_float2(tanh_approx(hh.x), tanh_approx(hh.y)), hh);
+      o[c] = pack_bf16x2(y.x, y.y);
     }
-    *reinterpret_cast<uint4*>(a1 + sw128_off(srow0 + i, c16, 128)) = pack8(y);
+    *reinterpret_cast<uint4*>(a1 + sw128_off(srow0 + i, c16, 128)) = out;
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
+    for (int c = 0; c < 4; ++c) {
       h0[c] = h1[c];
       h1[c] = h2[c];
       h2[c] = cur[c];
@@ -287,6 +299,7 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
   float* G2 = reinterpret_cast<float*>(sb + VEC);  // G * log2(e)
   float* bet = G2 + 64;                            // beta (0 past the chunk's length)
   float* fw = G2 + 128;                            // beta e^G
+  float* nG2 = G2 + 192;                           // -G * log2(e)
   float* Lf = reinterpret_cast<float*>(sb + LF);
   float* Tf = reinterpret_cast<float*>(sb + TF);
   const uint32_t bar0 = base + BARS;
@@ -366,6 +379,8 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
     const float G0 = incl - pair + a0, G1 = incl;  // natural-log cumsum at r0, r1
     G2[r0] = G0 * LOG2E;
     G2[r1] = G1 * LOG2E;
+    nG2[r0] = -(G0 * LOG2E);
+    nG2[r1] = -(G1 * LOG2E);
     bet[r0] = b0;
     bet[r1] = b1;
     fw[r0] = b0 * expf(G0);
@@ -403,31 +418,39 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
       uint4 u[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) u[j] = *reinterpret_cast<const uint4*>(sb + A1 + sw128_off(srow, part * 4 + j, 128));
-      float ss = 0.f;
+      // packed fp32 pipe (f32x2) for the sum of squares and both scalings
+      float2 ss2 = make_float2(0.f, 0.f);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        float f[8];
-        unpack8(u[j], f);
+        const __nv_bfloat162* hp = reinterpret_cast<const __nv_bfloat162*>(&u[j]);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) ss = fmaf(f[e], f[e], ss);
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(hp[e]);
+          ss2 = __ffma2_rn(f, f, ss2);
+        }
       }
+      float ss = ss2.x + ss2.y;
       ss += __shfl_xor_sync(0xffffffffu, ss, 1);
       ss += __shfl_xor_sync(0xffffffffu, ss, 2);
       const float inv = valid ? rsqrtf(ss + 1e-6f) * (rr ? scale : 1.0f) : 0.f;
       const float dec = rr ? exp2f(G2[row]) : exp2f(G2[63] - G2[row]);
+      const float2 inv2 = make_float2(inv, inv), dec2 = make_float2(dec, dec);
       uint4* gout = reinterpret_cast<uint4*>(tile + (rr ? OFF_QG : OFF_KG) + (size_t)row * 256 + part * 64);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        float f[8], d[8];
-        unpack8(u[j], f);
+        const __nv_bfloat162* hp = reinterpret_cast<const __nv_bfloat162*>(&u[j]);
+        uint4 nb, db;
+        uint32_t* np = reinterpret_cast<uint32_t*>(&nb);
+        uint32_t* dp = reinterpret_cast<uint32_t*>(&db);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) f[e] *= inv;
-        const uint4 nb = pack8(f);
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __fmul2_rn(__bfloat1622float2(hp[e]), inv2);
+          np[e] = pack_bf16x2(f.x, f.y);
+          const float2 d = __fmul2_rn(__bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&np[e])), dec2);
+          dp[e] = pack_bf16x2(d.x, d.y);
+        }
         *reinterpret_cast<uint4*>(sb + A1 + sw128_off(srow, part * 4 + j, 128)) = nb;
-        unpack8(nb, f);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) d[e] = f[e] * dec;
-        gout[j] = pack8(d);
+        gout[j] = db;
       }
     }
     fence_proxy_async_smem();
@@ -473,16 +496,33 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
     tmem_ld_wait();
     const int i = (q4 & 1) * 32 + lane;
     const float g2i = G2[i];
+    const float2 g2i2 = make_float2(g2i, g2i);
+    // decay e^(G_i - G_j) for the row's 32 columns j, pairs on the packed fp32 pipe
+    // (g2i + (-G_j) is the same rounding as g2i - G_j)
+    auto decay8 = [&](int j8, float2 (&e2)[4]) {
+      const float4 na = *reinterpret_cast<const float4*>(nG2 + chh * 32 + j8 * 8);
+      const float4 nc = *reinterpret_cast<const float4*>(nG2 + chh * 32 + j8 * 8 + 4);
+      const float2 d[4] = {__fadd2_rn(g2i2, make_float2(na.x, na.y)), __fadd2_rn(g2i2, make_float2(na.z, na.w)),
+                           __fadd2_rn(g2i2, make_float2(nc.x, nc.y)), __fadd2_rn(g2i2, make_float2(nc.z, nc.w))};
+#pragma unroll
+      for (int p = 0; p < 4; ++p) e2[p] = make_float2(ex2(d[p].x), ex2(d[p].y));
+    };
     if (q4 < 2) {
       const float nb = -bet[i];
+      const float2 nb2 = make_float2(nb, nb);
       float* dst = Lf + i * LDF + chh * 32;
 #pragma unroll
       for (int j8 = 0; j8 < 4; ++j8) {
+        float2 e2[4];
+        decay8(j8, e2);
         float l[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int j = chh * 32 + j8 * 8 + e;
-          l[e] = j < i ? nb * __uint_as_float(v[j8 * 8 + e]) * ex2(g2i - G2[j]) : 0.f;
+        for (int p = 0; p < 4; ++p) {
+          const float2 vv = make_float2(__uint_as_float(v[j8 * 8 + 2 * p]), __uint_as_float(v[j8 * 8 + 2 * p + 1]));
+          const float2 y = __fmul2_rn(__fmul2_rn(nb2, vv), e2[p]);
+          const int j = chh * 32 + j8 * 8 + 2 * p;
+          l[2 * p] = j < i ? y.x : 0.f;
+          l[2 * p + 1] = j + 1 < i ? y.y : 0.f;
         }
         *reinterpret_cast<float4*>(dst + j8 * 8) = make_float4(l[0], l[1], l[2], l[3]);
         *reinterpret_cast<float4*>(dst + j8 * 8 + 4) = make_float4(l[4], l[5], l[6], l[7]);
@@ -491,13 +531,18 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
       uint4* dst = reinterpret_cast<uint4*>(tile + OFF_A + (size_t)i * 128 + chh * 64);
 #pragma unroll
       for (int j8 = 0; j8 < 4; ++j8) {
-        float a[8];
+        float2 e2[4];
+        decay8(j8, e2);
+        uint4 out;
+        uint32_t* o = reinterpret_cast<uint32_t*>(&out);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int j = chh * 32 + j8 * 8 + e;
-          a[e] = j <= i ? __uint_as_float(v[j8 * 8 + e]) * ex2(g2i - G2[j]) : 0.f;
+        for (int p = 0; p < 4; ++p) {
+          const float2 vv = make_float2(__uint_as_float(v[j8 * 8 + 2 * p]), __uint_as_float(v[j8 * 8 + 2 * p + 1]));
+          const float2 y = __fmul2_rn(vv, e2[p]);
+          const int j = chh * 32 + j8 * 8 + 2 * p;
+          o[p] = pack_bf16x2(j <= i ? y.x : 0.f, j + 1 <= i ? y.y : 0.f);
         }
-        dst[j8] = pack8(a);
+        dst[j8] = out;
       }
     }
   }
@@ -505,33 +550,37 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
   __syncthreads();
 
   // 5. T = (I - L)^-1 in fp32.
-  //    Level 0 (warps 0-1, half a warp per diagonal block, lane = row): T_bb by row substitution
-  //    T_r = e_r + sum_{j<r} N_rj T_j with row j broadcast by shuffles once it is final.
+  //    Level 0 (warps 0-1, thread = one column k of one diagonal block b): forward substitution
+  //    down the column, x_r = d_rk + sum_{j<r} N_rj x_j with the FMAs in increasing j (the
+  //    reference's row-by-row update order); rows of N are shared-memory broadcasts within the
+  //    block's 16 threads and x stays in registers.
   //    Levels 1-3: 16x16 block products on the tensor cores (mma.sync tf32, 3xTF32 split,
   //    fp32-accurate): T_10 = T_11 L_10 T_00 and T_32 = T_33 L_32 T_22; then the 32x32 corner
   //    T_[23][01] = T_[23][23] (L_[23][01] T_[01][01]) as X = L T then Y = T X, four blocks each.
   //    Scratch: the unused upper blocks of L.
   if (ok && warp < 2) {
-    const int b = 2 * warp + (lane >> 4), r = lane & 15;
-    const float* nrow = Lf + (16 * b + r) * LDF + 16 * b;
-    float n[16], t[16];
+    const int b = tid >> 4, k = tid & 15;
+    const float* nb = Lf + (16 * b) * LDF + 16 * b;
+    float x[16];
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      n[k] = nrow[k];
-      t[k] = k == r ? 1.f : 0.f;
-    }
+    for (int r = 0; r < 16; ++r) {
+      float n[16];
 #pragma unroll
-    for (int j = 0; j < 15; ++j) {
-      const int src = (lane & 16) | j;
-#pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        const float tj = __shfl_sync(0xffffffffu, t[k], src);
-        if (r > j) t[k] = fmaf(n[j], tj, t[k]);
+      for (int j4 = 0; j4 < (r + 3) / 4; ++j4) {
+        const float4 q = *reinterpret_cast<const float4*>(nb + r * LDF + 4 * j4);
+        n[4 * j4] = q.x;
+        n[4 * j4 + 1] = q.y;
+        n[4 * j4 + 2] = q.z;
+        n[4 * j4 + 3] = q.w;
       }
-    }
-    float* trow = Tf + (16 * b + r) * LDF + 16 * b;
+      float acc = r == k ? 1.f : 0.f;
 #pragma unroll
-    for (int k = 0; k < 16; k += 4) *reinterpret_cast<float4*>(trow + k) = make_float4(t[k], t[k + 1], t[k + 2], t[k + 3]);
+      for (int j = 0; j < r; ++j) acc = fmaf(n[j], x[j], acc);
+      x[r] = acc;
+    }
+    float* tcol = Tf + (16 * b) * LDF + 16 * b + k;
+#pragma unroll
+    for (int r = 0; r < 16; ++r) tcol[r * LDF] = x[r];
   }
   __syncthreads();
   auto blk = [&](float* base_, int bi, int bj) { return base_ + (16 * bi) * LDF + 16 * bj; };
