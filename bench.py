@@ -41,8 +41,8 @@ REQUESTS_PER_GPU = 256  # config 5; --requests-per-gpu changes it only for small
 # batch 7 (32767 tokens; profiles/*.md give the commands); a launch's traffic is this times its
 # tokens (all these ops move bytes in proportion to the tokens they process).
 NCU_DRAM_BYTES_PER_TOKEN = {
-    "delta_rule": (475.78e6 + 575.00e6 + 625.47e6 + 118.14e6) / 32767,  # fused prep + recurrence
-    "gqa_attention": (282.43e6 + 96.97e6) / 32767,
+    "delta_rule": (482.46e6 + 578.07e6 + 625.41e6 + 118.64e6) / 32767,  # fused prep + recurrence
+    "gqa_attention": (284.16e6 + 96.58e6) / 32767,
     "packed_conv": (403.93e6 + 351.90e6) / 32767,
     "qk_norm_rope": (168.06e6 + 124.66e6) / 32767,
     "residual_rmsnorm": (402.88e6 + 345.73e6) / 32767,
