@@ -270,6 +270,52 @@ def cpu_reference_rate(model, cfg, requests, sample_ids, mean_flops, budget_s=20
     return rate, spent, tokens, n
 
 
+def reference_gpu_latency(cfg, weights, ids, dev, warmup=3, reps=10):
+    """The reference's own GPU forward, rerun on this GPU: transformers 5.5.0 Qwen3_5TextModel in bf16,
+    eager, with the kernels the reference environment binds where they install here (fla's Triton
+    chunked delta rule and gated RMSNorm when fla imports; torch conv1d, causal-conv1d being absent;
+    SDPA attention).  Batch 1, the config-4 request, hidden states only (no readout); CUDA events
+    around each forward after ``warmup`` untimed ones (the first compiles fla's Triton kernels)."""
+    from transformers.models.qwen3_5 import modeling_qwen3_5 as mq
+    old = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with torch.device(dev):
+            model = mq.Qwen3_5TextModel(cfg.to_transformers())
+    finally:
+        torch.set_default_dtype(old)
+    model.load_state_dict(weights, strict=True)
+    for i, kind in enumerate(cfg.layer_types):  # gate parameters stay float32, as in the checkpoint
+        if kind == "linear_attention":
+            la = model.layers[i].linear_attn
+            la.A_log.data = weights[f"layers.{i}.linear_attn.A_log"].float().to(dev)
+            la.dt_bias.data = weights[f"layers.{i}.linear_attn.dt_bias"].float().to(dev)
+    model.eval()
+    x = torch.tensor(ids[None].astype(np.int64), device=dev)
+    times = []
+    with torch.no_grad():
+        for i in range(warmup + reps):
+            s = torch.cuda.Event(enable_timing=True)
+            e = torch.cuda.Event(enable_timing=True)
+            s.record()
+            model(input_ids=x, use_cache=False)
+            e.record()
+            e.synchronize()
+            if i >= warmup:
+                times.append(s.elapsed_time(e))
+    del model, x
+    torch.cuda.empty_cache()
+    times.sort()
+    path = ("transformers 5.5.0 Qwen3_5TextModel bf16 eager on this GPU: "
+            + ("fla Triton chunked delta rule + gated RMSNorm" if mq.chunk_gated_delta_rule is not None
+               else "torch chunked delta rule") + ", "
+            + ("causal-conv1d" if mq.causal_conv1d_fn is not None else "torch conv1d + SiLU (causal-conv1d absent)")
+            + ", SDPA attention; the reference's own Triton packed-conv / native-GQA kernels are not used "
+              "(they hard-code an sm_89 launcher)")
+    return {"p50": statistics.median(times), "min": times[0], "p95": times[int(0.95 * (len(times) - 1))],
+            "reps": reps, "path": path}
+
+
 def cpu_sample_ids(requests, max_len=512, count=16):
     """Deterministic CPU sample: the first requests of the mix no longer than ``max_len`` tokens."""
     return [i for i, r in enumerate(requests) if r.ids.size <= max_len][:count]
@@ -460,6 +506,15 @@ def run_ours(args, world, rank, local):
                "tokens": b4.tokens, "tflops_p50": f4 / (statistics.median(times) / 1000) / 1e12,
                "frac_of_bf16_burst_peak": f4 / (statistics.median(times) / 1000) / 1e12 / pk["bf16_tflops"]}
 
+    # ---- the reference's GPU forward at config 4 on this GPU (N = 1 only)
+    ref_gpu = None
+    if world == 1 and lat is not None and not args.skip_ref_gpu:
+        try:
+            ref_gpu = reference_gpu_latency(cfg, weights, W.config4_request().ids, dev)
+            ref_gpu["speedup_p50"] = ref_gpu["p50"] / lat["p50"]
+        except Exception as exc:  # the GPU line must still print
+            ref_gpu = {"p50": None, "path": f"failed: {type(exc).__name__}: {exc}"}
+
     # ---- CPU reference baseline (rank 0, N = 1 only; bounded sample)
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
@@ -493,6 +548,7 @@ def run_ours(args, world, rank, local):
         "e2e": {"value": e2e_value, "unit": "requests/s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                 "api": "DecisionEngine.score(requests): batch planning and host packing overlapped with the device, pinned H2D, forward over two streams, D2H"},
         "latency_cfg4_ms": lat,
+        "reference_gpu_latency_cfg4_ms": ref_gpu,
         "gpu_launches": int(launches),
         "roofline": roof.get(dominant) if dominant else None,
         "roofline_kernels": {k: {kk: (round(vv, 4) if isinstance(vv, float) else vv) for kk, vv in v.items()}
@@ -519,6 +575,8 @@ def main():
     ap.add_argument("--requests-per-gpu", type=int, default=REQUESTS_PER_GPU)
     ap.add_argument("--skip-latency", action="store_true")
     ap.add_argument("--skip-e2e", action="store_true")
+    ap.add_argument("--skip-ref-gpu", action="store_true",
+                    help="skip timing the reference's transformers bf16 forward on this GPU at config 4")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--streams", type=int, default=2, help="CUDA streams the packed batches are spread over")
