@@ -40,6 +40,7 @@ SIGNATURES = {
     "fdk_attn_qk_norm_rope": (i32, [vp, i64, vp, vp, i32, vp, vp, i64, i32, vp, vp, i64, i64, i64, i64, f32, vp]),
     "fdk_gqa_fwd": (i32, [vp, i64, vp, i64, vp, i64, vp, i64, i64, i64, i64, i64, i64, f32, vp, i64, i32, vp, vp]),
     "fdk_poll_device_error": (i32, [C.POINTER(C.c_int)]),
+    "fdk_selftest_bounded_wait": (i32, [i64, vp]),
     "fdk_embed": (i32, [vp, vp, i64, i64, vp, i64, vp]),
     "fdk_swiglu": (i32, [vp, i64, vp, i64, i64, vp]),
     "fdk_slot_readout": (i32, [vp, i32, vp, i64, vp, vp, i64, vp, i32, vp, i64, f32, f32, vp, vp, vp]),

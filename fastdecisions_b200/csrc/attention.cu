@@ -398,6 +398,34 @@ extern "C" int fdk_gqa_fwd(const void* q, int64_t ld_q, const void* k, int64_t l
   return check_launch("gqa_fwd");
 }
 
+namespace fdk {
+namespace attn {
+// One warp waits on an mbarrier that nothing arrives on, through the same bounded wait every
+// kernel here uses; the wait runs out after `budget` SM cycles and bit 2 of the error word is set.
+__global__ void bounded_wait_probe_kernel(long long budget) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const bool ok = mbar_wait(smem_u32(&bar), 0, &abort_flag, budget);
+  if (__all_sync(0xffffffffu, ok ? 1 : 0) == 0 && threadIdx.x == 0) atomicOr(&g_device_error, 4);
+}
+}  // namespace attn
+}  // namespace fdk
+
+extern "C" int fdk_selftest_bounded_wait(int64_t budget_cycles, void* stream) {
+  if (budget_cycles <= 0 || budget_cycles > 4000000000LL)
+    return set_error(FDK_ERR_INVALID_ARGUMENT, "selftest_bounded_wait: budget_cycles must be in (0, 4e9]");
+  fdk::attn::bounded_wait_probe_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>((long long)budget_cycles);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(FDK_ERR_LAUNCH, cudaGetErrorString(e));
+  return FDK_OK;
+}
+
 extern "C" int fdk_poll_device_error(int* code) {
   int h = 0;
   if (cudaMemcpyFromSymbol(&h, fdk::attn::g_device_error, sizeof(int)) != cudaSuccess) {

@@ -225,6 +225,14 @@ int fdk_gqa_fwd(const void* q, int64_t ld_q, const void* k, int64_t ld_k, const 
  */
 int fdk_poll_device_error(int* code);
 
+/*
+ * Self-test of that failure path, with no GPU fault: one warp waits on an mbarrier that nothing
+ * arrives on, through the bounded wait the kernels use; after `budget_cycles` SM clock cycles
+ * (at most 4e9) the wait gives up, bit 2 (value 4) of the device error word is set and the
+ * kernel returns.  The context stays usable.  No reference counterpart.
+ */
+int fdk_selftest_bounded_wait(int64_t budget_cycles, void* stream);
+
 /* Token embedding gather: out[t, :] = table[ids[t], :] ([tf]:1243).  ids int32. */
 int fdk_embed(const int32_t* ids, const void* table, int64_t vocab, int64_t hidden, void* out,
               int64_t tokens, void* stream);

@@ -47,3 +47,10 @@ def test_ops_refuse_cpu_tensors():
         ops.residual_rmsnorm(x, x, w)
     with pytest.raises(ValueError):
         ops.packed_conv_qkv(torch.zeros(1, 8, 6144, dtype=torch.bfloat16), torch.zeros(6144, 4, dtype=torch.bfloat16))
+
+
+def test_selftest_budget_validated_before_launch():
+    # argument checks run on the host before any CUDA call, so this needs no GPU
+    for bad in (0, -5, 5_000_000_000):
+        with pytest.raises(ValueError, match="budget_cycles"):
+            _lib.call("fdk_selftest_bounded_wait", bad, None)
