@@ -54,3 +54,36 @@ def test_selftest_budget_validated_before_launch():
     for bad in (0, -5, 5_000_000_000):
         with pytest.raises(ValueError, match="budget_cycles"):
             _lib.call("fdk_selftest_bounded_wait", bad, None)
+
+
+def test_plain_c_host_compiles_links_and_calls(tmp_path):
+    """A C program (no C++, no CUDA headers) includes include/fdk.h, links libfdk.so and calls the
+    host-only entry points and one argument-checking failure path -- what a cgo / JNI host does."""
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc not available")
+    src = tmp_path / "host.c"
+    src.write_text(r'''
+#include <stdio.h>
+#include <string.h>
+#include "fdk.h"
+int main(void) {
+  const char* v = fdk_version();
+  size_t ws = fdk_chunk_gated_delta_rule_workspace_size(1536, 1, 16, 128, 128);
+  int st = fdk_selftest_bounded_wait(0, NULL);  /* rejected on the host, before any CUDA call */
+  printf("%s|%zu|%d|%s\n", v, ws, st, fdk_get_last_error_string());
+  return (strncmp(v, "fastdecisions-b200", 18) == 0 && ws > 0 && st == FDK_ERR_INVALID_ARGUMENT) ? 0 : 1;
+}
+''')
+    inc = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
+    libdir = os.path.dirname(_lib.LIB_PATH)
+    exe = tmp_path / "host"
+    subprocess.run([gcc, "-std=c99", "-Wall", "-Werror", "-I", inc, str(src), "-o", str(exe), "-L", libdir,
+                    "-l:libfdk.so", f"-Wl,-rpath,{libdir}"], check=True, capture_output=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout + r.stderr
+    version, ws, st, msg = r.stdout.strip().split("|")
+    assert int(ws) == _lib.load().fdk_chunk_gated_delta_rule_workspace_size(1536, 1, 16, 128, 128)
+    assert int(st) == _lib.FDK_ERR_INVALID_ARGUMENT and "budget_cycles" in msg
