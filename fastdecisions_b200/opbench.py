@@ -11,6 +11,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 
 import numpy as np
@@ -132,6 +133,36 @@ def time_op(fn, iters: int, warmup: int) -> float:
     return total / iters
 
 
+def time_rotating(fns, passes: int, warmup: int) -> float:
+    """Mean milliseconds per call over back-to-back calls that cycle through independent buffer
+    sets (their total far above L2, so every call streams from HBM).  One pass over the sets is
+    captured in a CUDA graph (warm-up on a side stream first) and replayed ``passes`` times between
+    two CUDA events: host dispatch is out of the measurement, as in the engine's graph replays."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(warmup):
+            for f in fns:
+                f()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for f in fns:
+            f()
+    graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(passes):
+        graph.replay()
+    e1.record()
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / (passes * len(fns))
+    del graph
+    return ms
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--op", default="all", help="one of %s, or all" % ", ".join(OPS))
@@ -140,19 +171,31 @@ def main(argv=None):
                     help="comma-separated request lengths to pack instead of a config-5 batch (e.g. 4096)")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--rotate-mb", type=int, default=0,
+                    help="HBM-bound ops: time CUDA-graph replays of back-to-back calls over enough "
+                         "independent buffer sets to move this many MB per pass (e.g. 1024, far above the "
+                         "126 MB L2) instead of single calls with an L2 flush between them")
     args = ap.parse_args(argv)
     cfg = ModelConfig()
     lens = [int(x) for x in args.lens.split(",")] if args.lens else batch_lengths(args.batch)
     peaks = _peaks()
     for op in (OPS if args.op == "all" else (args.op,)):
         fn, (bound, work) = make_case(op, lens, cfg)
-        ms = time_op(fn, args.iters, args.warmup)
+        timing = "single calls, L2 flushed between them"
+        if args.rotate_mb and bound == "hbm":
+            sets = max(2, math.ceil(args.rotate_mb * 2.0**20 / work))
+            fns = [fn] + [make_case(op, lens, cfg, seed=i)[0] for i in range(1, sets)]
+            ms = time_rotating(fns, args.iters, args.warmup)
+            timing = f"CUDA-graph replays, back-to-back over {sets} buffer sets ({sets * work / 2**20:.0f} MB a pass)"
+        else:
+            ms = time_op(fn, args.iters, args.warmup)
         achieved = work / (ms * 1e-3) / (1e12 if bound == "tensor" else 1e9)
         print(json.dumps({"op": op, "batch": "lens" if args.lens else args.batch, "tokens": int(sum(lens)),
                           "segments": len(lens),
                           "max_len": int(max(lens)), "us": round(ms * 1e3, 2), "bound": bound,
                           "achieved": round(achieved, 1), "unit": "TFLOP/s" if bound == "tensor" else "GB/s",
-                          "frac": round(achieved / peaks[bound], 4), "peak_source": peaks["source"]}), flush=True)
+                          "frac": round(achieved / peaks[bound], 4), "peak_source": peaks["source"],
+                          "timing": timing}), flush=True)
 
 
 if __name__ == "__main__":
