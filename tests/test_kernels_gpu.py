@@ -140,6 +140,17 @@ def test_packed_conv_varlen_and_strided_input():
     conv_compare(got, conv_ref(x, w, cu))
 
 
+@pytest.mark.parametrize("lens", [[1500, 900, 700], [4000, 1, 1999, 64]])  # two and four tiles a CTA
+def test_packed_conv_tiles_per_cta(lens):
+    g = gen(21)
+    T = sum(lens)
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32)
+    x = (torch.randn(1, T, 6144, generator=g) * 0.5).bfloat16()
+    w = (torch.randn(6144, 4, generator=g) * 0.25).bfloat16()
+    got = ops.packed_conv_qkv(dev(x), dev(w), cu_seqlens=dev(cu))
+    conv_compare(got, conv_ref(x, w, cu))
+
+
 def test_packed_conv_golden(golden):
     f = golden["conv"]
     x, w = f["x"], f["weight"]
