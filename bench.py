@@ -38,7 +38,7 @@ import torch  # noqa: E402
 REQUESTS_PER_GPU = 256  # config 5; --requests-per-gpu changes it only for small profiling runs
 
 # DRAM bytes (read + write) per token of one launch, from one ncu capture of each op on config-5
-# batch 7 (32767 tokens; profiles/*.md give the commands); a launch's traffic is this times its
+# batch 7 (32767 tokens; `ncu --set full` of `opbench --op <op> --batch 7`); a launch's traffic is this times its
 # tokens (all these ops move bytes in proportion to the tokens they process).
 NCU_DRAM_BYTES_PER_TOKEN = {
     "delta_rule": (482.46e6 + 578.07e6 + 625.41e6 + 118.64e6) / 32767,  # fused prep + recurrence
