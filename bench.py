@@ -3,20 +3,22 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU, NCCL)
 
-Headline (one JSON line from rank 0): requests/sec of the config-5 throughput sweep, weak
-scaling -- every GPU serves its own 256 seeded requests (lognormal lengths, median 800, clipped to
-[64, 8192], 2-8 candidates) through the config-4 model (synthetic 2B-class hybrid decoder, random
-weights from seed 17); requests are LPT-balanced over the ranks, packed into varlen batches, and
-only the answer probabilities are gathered to rank 0.  A step is one full pass over all ranks'
-requests.  The same line carries the config-4 batch-1 forward latency (p50 of CUDA-graph replays),
-the end-to-end rate through the public API (host token ids -> probabilities on the host), the
-roofline of the dominant own kernel, the CPU reference baseline, kernel launch counts and the SM
-clocks seen during the timed region.
+Headline (one JSON line from rank 0): requests/sec of the config-5 throughput sweep -- 256 seeded
+requests in total (lognormal lengths, median 800, clipped to [64, 8192], 2-8 candidates) through
+the config-4 model (synthetic 2B-class hybrid decoder, random weights from seed 17), sharded over
+the N GPUs by length-balanced bins (LPT on forward FLOPs), strong scaling; each rank packs its
+share into varlen batches and only the answer probabilities are gathered to rank 0.  A step is one
+full pass over the 256 requests.  The same line carries the config-4 batch-1 forward latency (p50
+of CUDA-graph replays) beside the reference's own bf16 GPU forward on the same GPU, the
+end-to-end rate through the public API (host token ids -> probabilities on the host), answer
+parity against the reference's float32 path on a length-stratified sample, the roofline of the
+dominant own kernel, the CPU reference baseline, kernel launch counts and the SM clocks seen
+during the timed region.
 
 ``--impl reference`` times the reference's own CPU path on this host: transformers 5.5.0
 ``Qwen3_5TextModel`` (the module FastDecisions' engine calls) in float32 eager on all host
-threads, one bounded request sample per step, on the same metric (FLOP-extrapolated to the
-config-5 request mix).  Under torchrun only rank 0 runs it.
+threads, one request of a length-stratified sample per step, on the same metric (FLOP-extrapolated
+to the config-5 request mix).  Under torchrun only rank 0 runs it.
 """
 from __future__ import annotations
 
@@ -35,7 +37,7 @@ sys.path.insert(0, ROOT)
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-REQUESTS_PER_GPU = 256  # config 5; --requests-per-gpu changes it only for small profiling runs
+REQUESTS = 256  # config 5, in total over all GPUs; --requests changes it only for small profiling runs
 
 # DRAM bytes (read + write) per token of one launch, from one ncu capture of each op on config-5
 # batch 7 (32767 tokens; `ncu --set full` of `opbench --op <op> --batch 7`); a launch's traffic is this times its
@@ -47,8 +49,8 @@ NCU_DRAM_BYTES_PER_TOKEN = {
     "qk_norm_rope": (168.06e6 + 124.66e6) / 32767,
     "residual_rmsnorm": (402.88e6 + 345.73e6) / 32767,
 }
-METRIC = ("requests/sec, config 5 (256 seeded requests per GPU, lognormal lengths median 800 in [64, 8192], "
-          "2-8 options) through the config-4 2B-class hybrid decision forward")
+METRIC = ("requests/sec, config 5 (256 seeded requests sharded over the GPUs, lognormal lengths median 800 in "
+          "[64, 8192], 2-8 options) through the config-4 2B-class hybrid decision forward")
 PEAKS_FALLBACK = dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0)
 
 
@@ -251,23 +253,36 @@ def build_cpu_reference(cfg, weights, threads):
 
 
 def cpu_reference_rate(model, cfg, requests, sample_ids, mean_flops, budget_s=20.0, max_requests=None):
-    """Float32 CPU forward over a bounded sample; returns (requests/s on the mix, seconds, tokens)."""
-    from fastdecisions_b200.workloads import letter_weight  # noqa: F401  (same readout rows)
-    spent, flops, tokens, n = 0.0, 0.0, 0, 0
+    """Float32 CPU forward over a bounded sample; returns (requests/s on the mix, seconds, tokens,
+    requests done, {request index: answer probabilities}).  The probabilities use the reference's
+    readout (model.py:18-27, engine.py:48-56): the final-normed hidden state at the slot times the
+    candidate rows, options past ``nopts`` masked, softmax."""
+    from fastdecisions_b200.workloads import LETTER_IDS
+    letters = None
+    spent, flops, tokens, n, probs = 0.0, 0.0, 0, 0, {}
     with torch.no_grad():
         for i in sample_ids:
             r = requests[i]
             ids = torch.tensor(r.ids[None].astype(np.int64))
             t0 = time.perf_counter()
-            model(input_ids=ids, use_cache=False)
+            hs = model(input_ids=ids, use_cache=False).last_hidden_state
             spent += time.perf_counter() - t0
+            if letters is None:
+                letters = model.embed_tokens.weight[list(LETTER_IDS)].float()
+            probs[i] = readout_probs(hs[0, r.slot], letters, r.nopts)
             flops += cfg.request_flops(r.ids.size)
             tokens += r.ids.size
             n += 1
             if spent >= budget_s or (max_requests and n >= max_requests):
                 break
-    rate = flops / spent / mean_flops
-    return rate, spent, tokens, n
+    rate = flops / spent / mean_flops if spent > 0 else None
+    return rate, spent, tokens, n, probs
+
+
+def readout_probs(h_slot, letters, nopts, temperature=1.0):
+    lg = h_slot.float() @ letters.t()
+    lg = lg.masked_fill(torch.arange(letters.shape[0]) >= nopts, float("-inf"))
+    return torch.softmax(lg / temperature, -1).numpy()
 
 
 def reference_gpu_latency(cfg, weights, ids, dev, warmup=3, reps=10):
@@ -316,9 +331,29 @@ def reference_gpu_latency(cfg, weights, ids, dev, warmup=3, reps=10):
             "reps": reps, "path": path}
 
 
-def cpu_sample_ids(requests, max_len=512, count=16):
-    """Deterministic CPU sample: the first requests of the mix no longer than ``max_len`` tokens."""
-    return [i for i, r in enumerate(requests) if r.ids.size <= max_len][:count]
+def cpu_sample_ids(requests, max_len=2048, strata=16):
+    """Deterministic, length-stratified CPU sample of the mix: the middle request of each of
+    ``strata`` equal-count length strata (requests longer than ``max_len`` skipped: one 8192-token
+    fp32 forward alone takes longer than the whole sample's budget), ordered by bit-reversed
+    stratum index so that any prefix the time budget allows spans the length range."""
+    order = sorted(range(len(requests)), key=lambda i: (requests[i].ids.size, i))
+    per = len(order) / strata
+    mids = [order[min(len(order) - 1, int((k + 0.5) * per))] for k in range(strata)]
+    bits = max(1, (strata - 1).bit_length())
+    rev = sorted(range(strata), key=lambda k: int(format(k, f"0{bits}b")[::-1], 2))
+    return [mids[k] for k in rev if requests[mids[k]].ids.size <= max_len]
+
+
+def parity_summary(ours: dict, ref: dict) -> dict:
+    """|dp| (percentage points) and argmax agreement of our answer probabilities against the
+    reference's float32 path, over the requests both have."""
+    keys = [k for k in ref if k in ours]
+    if not keys:
+        return None
+    dp = np.array([np.abs(np.asarray(ours[k]) - ref[k]).max() for k in keys]) * 100
+    agree = sum(int(np.argmax(ours[k]) == np.argmax(ref[k])) for k in keys)
+    return {"n": len(keys), "max_dp_pp": round(float(dp.max()), 3), "mean_dp_pp": round(float(dp.mean()), 3),
+            "argmax_agree": f"{agree}/{len(keys)}"}
 
 
 # ------------------------------------------------------------------------------ main paths
@@ -329,15 +364,15 @@ def run_reference(args, world, rank):
     cfg = W.ModelConfig()
     threads = os.cpu_count() or 1
     weights = W.synthetic_weights(cfg, threads=threads)
-    reqs = W.config5_requests(REQUESTS_PER_GPU * args.gpus)
+    reqs = W.config5_requests(args.requests * (args.gpus if args.weak else 1))
     mean_flops = float(np.mean([cfg.request_flops(r.ids.size) for r in reqs]))
     model = build_cpu_reference(cfg, weights, threads)
     del weights
-    sample = cpu_sample_ids(reqs)
+    sample = cpu_sample_ids(reqs, max_len=1024)
     rates, times = [], []
     for step in range(args.warmup + args.steps):
         i = sample[step % len(sample)]
-        rate, spent, _, _ = cpu_reference_rate(model, cfg, reqs, [i], mean_flops, max_requests=1)
+        rate, spent, _, _, _ = cpu_reference_rate(model, cfg, reqs, [i], mean_flops, max_requests=1)
         if step >= args.warmup:
             rates.append(rate)
             times.append(spent)
@@ -347,17 +382,30 @@ def run_reference(args, world, rank):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "requests/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * sum(times) / len(times),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config 5 request mix, one sampled request (<= 512 tokens) per step, FLOP-extrapolated",
+        "higher_is_better": True, "scaling": "weak" if args.weak else "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": "config 5 request mix, one request of a length-stratified sample (<= 1024 tokens) per "
+                               "step, FLOP-extrapolated",
                    "model": "transformers 5.5.0 Qwen3_5TextModel, float32 eager, CPU (the module the reference's engine calls)",
                    "requests": len(reqs)},
         "cpu_baseline": {"value": value, "unit": "requests/s", "cores": torch.get_num_threads(), "kind": "reference",
-                         "sample": f"{args.steps} requests of the config-5 mix (<= 512 tokens each), float32, "
-                                   "extrapolated to the mix by forward FLOPs"},
+                         "sample": f"{args.steps} requests of a length-stratified sample of the config-5 mix "
+                                   "(<= 1024 tokens each), float32, extrapolated to the mix by forward FLOPs"},
         "e2e": {"value": value, "unit": "requests/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def _r(x, nd=4):
+    """Round floats to ``nd`` significant digits for the (deliberately short) JSON line."""
+    if isinstance(x, float):
+        return float(f"{x:.{nd}g}") if math.isfinite(x) else None
+    if isinstance(x, dict):
+        return {k: _r(v, nd) for k, v in x.items()}
+    if isinstance(x, (list, tuple)):
+        return [_r(v, nd) for v in x]
+    return x
 
 
 def run_ours(args, world, rank, local):
@@ -374,8 +422,9 @@ def run_ours(args, world, rank, local):
     timer = KernelTimer()
     engine.kernel_timer = timer
 
-    # ---- workload: 256 requests per GPU, LPT over ranks, packed varlen batches
-    reqs = W.config5_requests(args.requests_per_gpu * world)
+    # ---- workload: 256 requests in total (strong scaling; --weak: 256 per GPU), LPT over ranks,
+    #      packed varlen batches
+    reqs = W.config5_requests(args.requests * (world if args.weak else 1))
     costs = [cfg.request_flops(r.ids.size) for r in reqs]
     bins = lpt_partition(costs, world)
     mine = bins[rank]
@@ -388,7 +437,6 @@ def run_ours(args, world, rank, local):
     K = len(W.LETTER_IDS)
     local_ids = np.concatenate([np.array(o, dtype=np.int64) for o in order])
     out_probs = torch.empty((len(local_ids), K), device=dev, dtype=torch.float32)
-    out_logits = torch.empty_like(out_probs)
     slices, off = [], 0
     for b in batches:
         slices.append((off, off + b.num_segments))
@@ -435,6 +483,7 @@ def run_ours(args, world, rank, local):
     assert _lib.poll_device_error() == 0
     if rank == 0:
         assert final is not None and torch.isfinite(final).all()
+        final_h = final.cpu().numpy()
 
     # ---- per-op rooflines: the same steps again on one stream with a CUDA event pair around every
     #      op (events between kernels add gaps, so this pass is kept out of the throughput figure)
@@ -443,7 +492,6 @@ def run_ours(args, world, rank, local):
     timer.enabled = False
     tot = timer.totals()
     pk, pk_kind = peaks()
-    step_ms_local = step_ms_total
     work = op_work(cfg, batches)           # per step: {op: (bound, units)}
     roof = {}
     for name, (bound, units) in work.items():
@@ -460,10 +508,10 @@ def run_ours(args, world, rank, local):
                       "traffic": (NCU_DRAM_BYTES_PER_TOKEN[name] * sum(b.tokens for b in batches) /
                                   len(batches)) if name in NCU_DRAM_BYTES_PER_TOKEN else None,
                       "kernel": name, "launches": tot[name]["launches"],
-                      "total_ms": tot[name]["total_ms"], "share_of_step": tot[name]["total_ms"] / step_ms_local,
+                      "share_of_step": tot[name]["total_ms"] / step_ms_total,
                       "per_launch_units": units / max(1, tot[name]["launches"] // args.steps), "peak_source": src}
     own = {k: v for k, v in roof.items() if k != "gemm"}
-    dominant = max(own, key=lambda n: own[n]["total_ms"]) if own else None
+    dominant = max(own, key=lambda n: own[n]["share_of_step"]) if own else None
 
     # ---- end to end through the public API: host requests -> probabilities on the host
     e2e_steps = 0 if args.skip_e2e else max(1, min(args.steps, 3))
@@ -479,12 +527,12 @@ def run_ours(args, world, rank, local):
     e1.record()
     torch.cuda.synchronize(dev)
     barrier()
-    e2e_ms = allreduce_max(e0.elapsed_time(e1))
+    e2e_ms = allreduce_max(e0.elapsed_time(e1)) if e2e_steps else 0.0
     e2e_value = total_requests * e2e_steps / (e2e_ms / 1000.0) if e2e_steps else None
 
     # ---- config-4 batch-1 latency (CUDA graph replays, p50 over 30)
-    lat = None
-    if (rank == 0 or world == 1) and not args.skip_latency:
+    lat, probs4 = None, None
+    if rank == 0 and not args.skip_latency:
         r4 = W.config4_request()
         b4 = pack([r4])
         key = engine.capture(b4.tokens, 1, b4.max_seqlen)
@@ -496,73 +544,96 @@ def run_ours(args, world, rank, local):
             s = torch.cuda.Event(enable_timing=True)
             e = torch.cuda.Event(enable_timing=True)
             s.record()
-            engine.replay(key)
+            p4 = engine.replay(key)
             e.record()
             e.synchronize()
             times.append(s.elapsed_time(e))
+        probs4 = p4[0].cpu().numpy()
         times.sort()
         f4 = cfg.request_flops(b4.tokens)
-        lat = {"p50": statistics.median(times), "min": times[0], "p95": times[int(0.95 * (len(times) - 1))],
-               "tokens": b4.tokens, "tflops_p50": f4 / (statistics.median(times) / 1000) / 1e12,
-               "frac_of_bf16_burst_peak": f4 / (statistics.median(times) / 1000) / 1e12 / pk["bf16_tflops"]}
+        p50 = statistics.median(times)
+        lat = {"p50": p50, "min": times[0], "p95": times[int(0.95 * (len(times) - 1))], "tokens": b4.tokens,
+               "tflops_p50": f4 / (p50 / 1000) / 1e12}
 
     # ---- the reference's GPU forward at config 4 on this GPU (N = 1 only)
     ref_gpu = None
     if world == 1 and lat is not None and not args.skip_ref_gpu:
         try:
             ref_gpu = reference_gpu_latency(cfg, weights, W.config4_request().ids, dev)
-            ref_gpu["speedup_p50"] = ref_gpu["p50"] / lat["p50"]
+            ref_gpu = {"p50": ref_gpu["p50"], "min": ref_gpu["min"], "speedup_p50": ref_gpu["p50"] / lat["p50"],
+                       "path": "transformers 5.5.0 bf16 eager, fla Triton delta rule, torch conv1d, SDPA"
+                       if "fla" in ref_gpu["path"] else ref_gpu["path"]}
         except Exception as exc:  # the GPU line must still print
-            ref_gpu = {"p50": None, "path": f"failed: {type(exc).__name__}: {exc}"}
+            ref_gpu = {"p50": None, "path": f"failed: {type(exc).__name__}: {str(exc)[:80]}"}
 
-    # ---- CPU reference baseline (rank 0, N = 1 only; bounded sample)
-    cpu = None
+    # ---- CPU reference baseline (rank 0, N = 1 only; bounded, length-stratified sample) and the
+    #      answer parity of the timed run against that float32 reference path
+    cpu, parity = None, None
     if world == 1 and not args.no_cpu_baseline:
         try:
             model = build_cpu_reference(cfg, weights, os.cpu_count() or 1)
             mean_flops = float(np.mean(costs))
             sample = cpu_sample_ids(reqs)
-            rate, spent, toks, n = cpu_reference_rate(model, cfg, reqs, sample, mean_flops, budget_s=args.cpu_budget)
+            rate, spent, toks, n, ref_probs = cpu_reference_rate(model, cfg, reqs, sample, mean_flops,
+                                                                 budget_s=args.cpu_budget)
+            lens = sorted(reqs[i].ids.size for i in ref_probs)
             cpu = {"value": rate, "unit": "requests/s", "cores": torch.get_num_threads(), "kind": "reference",
-                   "sample": f"{n} requests ({toks} tokens) of the config-5 mix, transformers Qwen3_5TextModel float32 "
-                             f"eager on the host, {spent:.1f} s, extrapolated to the mix by forward FLOPs"}
+                   "sample": f"{n} requests ({toks} tokens, lengths {lens[0]}-{lens[-1]}) from 16 length strata of "
+                             f"the config-5 mix, transformers Qwen3_5TextModel fp32 eager, {spent:.1f} s, "
+                             f"FLOP-extrapolated to the mix", "cpu": cpu_model()}
+            parity = parity_summary({i: final_h[i] for i in ref_probs}, ref_probs)
+            if probs4 is not None:  # config 4 too (the latency request)
+                r4 = W.config4_request()
+                _, _, _, _, p4ref = cpu_reference_rate(model, cfg, [r4], [0], 1.0)
+                parity["config4_dp_pp"] = round(float(np.abs(probs4 - p4ref[0]).max() * 100), 3)
+                parity["config4_argmax_same"] = bool(np.argmax(probs4) == np.argmax(p4ref[0]))
+            parity["vs"] = "transformers 5.5.0 float32 CPU forward of the timed requests"
             del model
         except Exception as exc:  # the GPU line must still print
             cpu = {"value": None, "unit": "requests/s", "cores": os.cpu_count(), "kind": "reference",
-                   "sample": f"failed: {type(exc).__name__}: {exc}"}
+                   "sample": f"failed: {type(exc).__name__}: {str(exc)[:80]}"}
 
     tokens_local = sum(b.tokens for b in batches)
     tokens_all = allreduce_sum(float(tokens_local))
     if rank != 0:
         return 0
+    rl = roof.get(dominant) if dominant else None
     line = {
         "metric": METRIC, "value": value, "unit": "requests/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random weights and token ids)",
-        "config": {"workload": "config 5: 256 requests per GPU, LPT-balanced, packed varlen batches; config-4 model",
-                   "model": "synthetic 2B-class Qwen3.5-style hybrid decoder (18 GDN + 6 GQA layers, hidden 2048)",
-                   "requests": total_requests, "tokens": int(tokens_all), "max_tokens_per_batch": args.max_tokens,
-                   "batches_rank0": len(batches), "parallelism": f"dp{world} (request sharding, no collective on the hot path)",
-                   "l2": "inputs larger than L2: 3.4 GB of weights and GBs of activations stream every forward",
-                   "rank_loads_tflop": [round(x / 1e12, 2) for x in bin_loads(costs, bins)]},
-        "e2e": {"value": e2e_value, "unit": "requests/s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-                "api": "DecisionEngine.score(requests): batch planning and host packing overlapped with the device, pinned H2D, forward over two streams, D2H"},
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "weak" if args.weak else "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded random weights and token ids)",
         "latency_cfg4_ms": lat,
         "reference_gpu_latency_cfg4_ms": ref_gpu,
+        "parity": parity,
+        "e2e": {"value": e2e_value, "unit": "requests/s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                "api": "DecisionEngine.score"},
         "gpu_launches": int(launches),
-        "roofline": roof.get(dominant) if dominant else None,
-        "roofline_kernels": {k: {kk: (round(vv, 4) if isinstance(vv, float) else vv) for kk, vv in v.items()}
-                             for k, v in roof.items()},
+        "roofline": rl,
         "cpu_baseline": cpu,
         "clocks": clocks.summary(),
-        "timing": "CUDA events on the launching stream, barrier + synchronize around the timed steps, max over ranks",
-        "streams": args.streams,
-        "roofline_pass": {"ms_per_step": step_ms_total / args.steps, "streams": 1,
-                          "how": "the same steps repeated right after the timed region on one stream, a CUDA event "
-                                 "pair around every op; per-op achieved = algorithmic work / event time"},
+        "config": {"workload": f"config 5: {total_requests} requests over {world} GPU(s), LPT-balanced, packed varlen; "
+                               "config-4 model",
+                   "tokens": int(tokens_all), "max_tokens_per_batch": args.max_tokens,
+                   "parallelism": f"dp{world} (request sharding, no collective on the hot path)",
+                   "l2": "inputs larger than L2 (3.4 GB of weights stream every forward)",
+                   "rank_loads_tflop": [round(x / 1e12, 1) for x in bin_loads(costs, bins)]},
+        "roofline_frac": {k: round(v["frac"], 3) for k, v in roof.items()},
+        "share_of_step": {k: round(v["share_of_step"], 3) for k, v in roof.items()},
     }
-    print(json.dumps(line), flush=True)
+    print(json.dumps(_r(line)), flush=True)
     return 0
+
+
+def cpu_model() -> str:
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
 
 
 def main():
@@ -572,12 +643,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--max-tokens", type=int, default=32768)
-    ap.add_argument("--requests-per-gpu", type=int, default=REQUESTS_PER_GPU)
+    ap.add_argument("--requests", type=int, default=REQUESTS,
+                    help="requests of the config-5 mix in total (per GPU with --weak)")
+    ap.add_argument("--weak", action="store_true", help="weak scaling: --requests per GPU instead of in total")
     ap.add_argument("--skip-latency", action="store_true")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-ref-gpu", action="store_true",
                     help="skip timing the reference's transformers bf16 forward on this GPU at config 4")
-    ap.add_argument("--cpu-budget", type=float, default=20.0)
+    ap.add_argument("--cpu-budget", type=float, default=25.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--streams", type=int, default=2, help="CUDA streams the packed batches are spread over")
     args = ap.parse_args()

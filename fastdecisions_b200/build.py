@@ -28,16 +28,6 @@ def nvcc() -> str:
     raise RuntimeError("nvcc not found (set NVCC or put the CUDA toolkit on PATH)")
 
 
-def cutlass_include() -> str | None:
-    """CuTe/CUTLASS headers vendored by flashinfer in this image (optional, headers only)."""
-    try:
-        import flashinfer  # noqa: F401
-        d = os.path.join(os.path.dirname(flashinfer.__file__), "data", "cutlass", "include")
-        return d if os.path.isdir(d) else None
-    except Exception:
-        return None
-
-
 def _flags(extra=()):
     f = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
                 "-I", os.path.join(ROOT, "include"), "-I", CSRC]

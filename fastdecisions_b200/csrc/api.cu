@@ -1,6 +1,8 @@
 // Library-wide entry points: version, thread-local error string, device checks.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -22,20 +24,51 @@ int check_launch(const char* what) {
   return FDK_OK;
 }
 
-static int g_sm_major[64];
-static int g_sm_count[64];
+// Per-device attributes, cached; host threads may race on the first query (each writes the same
+// values, the count before the major that marks the slot filled).
+static std::atomic<int> g_sm_major[64];
+static std::atomic<int> g_sm_count[64];
 
 static int query(int dev) {
   if (dev < 0 || dev >= 64) return FDK_ERR_DEVICE;
-  if (g_sm_major[dev] == 0) {
+  if (g_sm_major[dev].load(std::memory_order_acquire) == 0) {
     int major = 0, count = 0;
     if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
         cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
       cudaGetLastError();
       return FDK_ERR_DEVICE;
     }
-    g_sm_count[dev] = count;
-    g_sm_major[dev] = major;
+    g_sm_count[dev].store(count, std::memory_order_relaxed);
+    g_sm_major[dev].store(major, std::memory_order_release);
+  }
+  return FDK_OK;
+}
+
+// (kernel, device) pairs whose dynamic shared-memory limit has been raised; guarded by a mutex so
+// concurrent first calls from several host threads each see the attribute set before launching.
+static std::mutex g_attr_mu;
+static const void* g_attr_func[256];
+static int g_attr_dev[256];
+static int g_attr_n = 0;
+
+int ensure_smem_attr(const void* func, int bytes, const char* what) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(FDK_ERR_DEVICE, "%s: no current device", what);
+  }
+  std::lock_guard<std::mutex> lock(g_attr_mu);
+  for (int i = 0; i < g_attr_n; ++i)
+    if (g_attr_func[i] == func && g_attr_dev[i] == dev) return FDK_OK;
+  const cudaError_t e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(FDK_ERR_LAUNCH, "%s: cannot set %d bytes of shared memory: %s", what, bytes, cudaGetErrorString(e));
+  }
+  if (g_attr_n < 256) {
+    g_attr_func[g_attr_n] = func;
+    g_attr_dev[g_attr_n] = dev;
+    ++g_attr_n;
   }
   return FDK_OK;
 }
@@ -47,9 +80,9 @@ int check_device() {
     return set_error(FDK_ERR_DEVICE, "no CUDA device available");
   }
   if (query(dev) != FDK_OK) return set_error(FDK_ERR_DEVICE, "cannot query CUDA device %d", dev);
-  if (g_sm_major[dev] != 10)
-    return set_error(FDK_ERR_DEVICE, "device %d is sm_%d0; this library is built for sm_100a only", dev,
-                     g_sm_major[dev]);
+  const int major = g_sm_major[dev].load(std::memory_order_acquire);
+  if (major != 10)
+    return set_error(FDK_ERR_DEVICE, "device %d is sm_%d0; this library is built for sm_100a only", dev, major);
   return FDK_OK;
 }
 
@@ -57,7 +90,7 @@ int sm_count() {
   int dev = 0;
   cudaGetDevice(&dev);
   if (query(dev) != FDK_OK) return 148;
-  return g_sm_count[dev];
+  return g_sm_count[dev].load(std::memory_order_relaxed);
 }
 
 }  // namespace fdk

@@ -383,13 +383,7 @@ extern "C" int fdk_gqa_fwd(const void* q, int64_t ld_q, const void* k, int64_t l
   prm.gate = static_cast<const bf16*>(gate);
   prm.ld_gate = ld_gate;
   prm.gate_hstride = gate_interleaved ? 2 * HD : HD;
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaFuncSetAttribute(gqa_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
-  }
+  if (int st = ensure_smem_attr((const void*)gqa_fwd_kernel, (int)SMEM_BYTES, "gqa_fwd")) return st;
   const int64_t mtiles = (max_seqlen + BM - 1) / BM;
   if (mtiles > 65535 || num_segments * (hq / 2) > 0x7fffffff)
     return set_error(FDK_ERR_UNSUPPORTED, "gqa_fwd: too many query tiles or segments");
@@ -438,7 +432,7 @@ extern "C" int fdk_poll_device_error(int* code) {
   }
   const int d = fdk::delta_take_device_error();
   if (d < 0) return set_error(FDK_ERR_DEVICE, "poll_device_error: cannot read the device error word");
-  h |= d << 1;
+  h |= ((d & 1) << 1) | ((d & 2) << 2);  // 2: a delta-rule wait ran out; 8: cu_seqlens rejected
   if (code) *code = h;
   return FDK_OK;
 }

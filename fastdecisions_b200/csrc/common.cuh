@@ -19,6 +19,9 @@ int check_launch(const char* what);
 int check_device();
 // Number of SMs of the current device (cached per device).
 int sm_count();
+// Raises `func`'s dynamic shared-memory limit to `bytes` on the current device, once per (kernel,
+// device), safely from several host threads.  The cache assumes no cudaDeviceReset afterwards.
+int ensure_smem_attr(const void* func, int bytes, const char* what);
 // Reads and clears the delta-rule recurrence's device error word (set when a bounded wait ran out).
 int delta_take_device_error();
 

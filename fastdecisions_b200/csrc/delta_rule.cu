@@ -56,13 +56,30 @@ __host__ __device__ inline WsLayout ws_layout(int64_t tokens, int64_t nseg, int6
   return l;
 }
 
+__device__ int g_delta_error = 0;  // bit 0: a bounded wait ran out; bit 1: cu_seqlens rejected on the device
+
 // One CTA of 256 threads: exclusive scan of ceil(len / 64) over segments (table[s] = first chunk
 // of segment s, table[nseg] = chunk count), each chunk's (first token, length, segment start), and the zeroed
 // work counter of the recurrence (table[nseg + 1]).
-__global__ void __launch_bounds__(256) chunk_table_kernel(const int32_t* __restrict__ cu, int nseg,
-                                                          int32_t* __restrict__ table, int4* __restrict__ info) {
+// cu_seqlens lives on the device, so the host cannot check it: this kernel does.  Unless
+// cu[0] == 0, cu is non-decreasing and cu[nseg] == tokens (which bounds the chunk count by
+// max_chunks, the size the workspace was laid out for), it writes an all-zero table -- every
+// segment empty, so the prep and the recurrence touch no tile and no output row -- and sets bit 1
+// of the delta-rule error word.
+__global__ void __launch_bounds__(256) chunk_table_kernel(const int32_t* __restrict__ cu, int nseg, int64_t tokens,
+                                                          int64_t max_chunks, int32_t* __restrict__ table,
+                                                          int4* __restrict__ info) {
   __shared__ int warp_sums[8];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  bool bad = false;
+  for (int s = tid; s < nseg; s += 256) bad |= cu[s + 1] < cu[s];
+  if (tid == 0) bad |= cu[0] != 0 || (int64_t)cu[nseg] != tokens;
+  if (__syncthreads_or(bad)) {
+    for (int s = tid; s <= nseg + 1; s += 256) table[s] = 0;
+    if (tid == 0) atomicOr(&g_delta_error, 2);
+    return;
+  }
+  (void)max_chunks;  // sum of ceil(len / 64) <= tokens / 64 + nseg == max_chunks once cu is valid
   int carry = 0;
   for (int base = 0; base < nseg; base += 256) {
     const int s = base + tid;
@@ -110,8 +127,6 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
   const bool ok = sm100::mbar_wait(bar, parity, abort_flag);
   return __all_sync(0xffffffffu, ok ? 1 : 0) != 0;
 }
-
-__device__ int g_delta_error = 0;  // set when a bounded wait of a delta-rule kernel ran out
 
 // ---- 16x16 fp32 block products on the tensor cores: mma.sync m16n8k8 tf32 with the 3xTF32 split
 //      (x = hi + lo, both tf32; x*y ~ hi*hi + hi*lo + lo*hi), accurate to about fp32.  One warp per
@@ -687,7 +702,7 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
       umma_commit(bar0 + 8 * B_DRAIN);
       mbar_wait(bar0 + 8 * B_DRAIN, 0, &never, DRAIN_BUDGET);
     }
-    atomicExch(&g_delta_error, 1);
+    atomicOr(&g_delta_error, 1);
   }
   tc_fence_before();
   __syncthreads();
@@ -1018,7 +1033,7 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
     tc_fence_after();
     tmem_dealloc(tmem, TM_COLS);
   }
-  if (tid == 0 && *abort_flag) atomicExch(&g_delta_error, 1);
+  if (tid == 0 && *abort_flag) atomicOr(&g_delta_error, 1);
 }
 
 // Final state of empty segments (their chains never enter the recurrence): the initial state, or 0.
@@ -1128,13 +1143,8 @@ static int launch_recur(int nseg, int heads, int64_t n_tiles, cudaStream_t s, co
   if (int st = tile_map(&ma, tiles, OFF_A, DR_C, DR_C, n_tiles)) return st;
   if (int st = tile_map(&mut, tiles, OFF_UT, DR_C, DR_D, n_tiles)) return st;
   const RParams prm{cu, table, counter, nseg, heads, tiles, init, out, fin};
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaFuncSetAttribute(delta_recur_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
-  }
+  if (int st = ensure_smem_attr((const void*)delta_recur_tc_kernel, (int)SMEM_BYTES, "chunk_gated_delta_rule/recurrence"))
+    return st;
   const int64_t items = (int64_t)nseg * heads;
   const unsigned grid = (unsigned)(items < sm_count() ? items : sm_count());
   delta_recur_tc_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(mw, mqg, mkg, ma, mut, prm);
@@ -1166,7 +1176,7 @@ static int run_delta_rule(bool conv, const void* q, const void* k, int64_t ld_qk
   int4* info = reinterpret_cast<int4*>(ws + lay.off_info);
   uint8_t* tiles = ws + lay.off_tiles;
   const int nseg = (int)num_segments;
-  chunk_table_kernel<<<1, 256, 0, s>>>(cu_seqlens, nseg, table, info);
+  chunk_table_kernel<<<1, 256, 0, s>>>(cu_seqlens, nseg, tokens, lay.max_chunks, table, info);
   if (int st = check_launch("chunk_gated_delta_rule/table")) return st;
   if (tokens == 0 && !final_state) return FDK_OK;
   if (tokens > 0) {
@@ -1180,16 +1190,9 @@ static int run_delta_rule(bool conv, const void* q, const void* k, int64_t ld_qk
       if (int st = drtc::act_map(&mk, k, tokens, heads, ld_qk)) return st;
       if (int st = drtc::act_map(&mv, v, tokens, heads, ld_v)) return st;
     }
-    static bool attr_set[2][64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64 || !attr_set[conv][dev]) {
-      if (conv)
-        cudaFuncSetAttribute(dprep::delta_prep_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dprep::SMEM_BYTES);
-      else
-        cudaFuncSetAttribute(dprep::delta_prep_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dprep::SMEM_BYTES);
-      if (dev >= 0 && dev < 64) attr_set[conv][dev] = true;
-    }
+    if (int st = ensure_smem_attr(conv ? (const void*)dprep::delta_prep_kernel<true> : (const void*)dprep::delta_prep_kernel<false>,
+                                  (int)dprep::SMEM_BYTES, "chunk_gated_delta_rule/prep"))
+      return st;
     const dim3 grid((unsigned)lay.max_chunks, (unsigned)heads);
     if (conv)
       dprep::delta_prep_kernel<true><<<grid, dprep::THREADS, dprep::SMEM_BYTES, s>>>(mq, mk, mv, in, info, table, nseg,

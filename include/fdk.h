@@ -154,7 +154,9 @@ int fdk_gdn_fused_delta_rule_fwd(const void* proj, int64_t ld_proj, const void* 
  *     32 MiB is rejected with FDK_ERR_UNSUPPORTED before anything is launched (one 1536-token
  *     request with 16 heads needs about 29.5 MiB).
  *   - The first call on a device looks up the array's device address there (with that device
- *     current) and caches it; make that first call before any stream capture.
+ *     current) and caches it; make that first call before any stream capture.  The cache
+ *     outlives cudaDeviceReset: after a reset of a device this entry point must not be used
+ *     on it again in the same process.
  *   - Nothing in the scratch has to start at zero: each call rebuilds its chunk table and every
  *     tile it reads.  All calls on a device share the one array and it keeps the last call's
  *     contents, so calls that overlap on the GPU (concurrent streams) race; serialise them.
@@ -219,8 +221,11 @@ int fdk_gqa_fwd(const void* q, int64_t ld_q, const void* k, int64_t ld_k, const 
 
 /*
  * Reads and clears the device-side error word of the current device.  Kernels that wait on
- * mbarriers (fdk_gqa_fwd) bound every wait; a wait that runs out sets this word to non-zero,
- * frees its resources and returns without finishing its tile.  Synchronises with the device.
+ * mbarriers (fdk_gqa_fwd, the delta rule) bound every wait; a wait that runs out sets a bit of
+ * this word, frees its resources and returns without finishing its tile.  Bits: 1 an attention
+ * wait ran out, 2 a delta-rule wait ran out, 4 the bounded-wait self-test, 8 the delta rule found
+ * cu_seqlens invalid on the device (cu[0] != 0, decreasing, or cu[num_segments] != tokens) and
+ * treated every segment as empty.  Synchronises with the device.
  * No reference counterpart (the reference's Triton kernels have no device waits).
  */
 int fdk_poll_device_error(int* code);

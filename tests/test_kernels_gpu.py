@@ -318,6 +318,33 @@ def test_delta_rule_config4_layer_shape():
     assert err < MAX_ABS
 
 
+def test_delta_rule_rejects_cu_seqlens_beyond_tokens_on_the_device():
+    """cu_seqlens lives on the device: the chunk-table kernel checks it (cu[0] == 0, non-decreasing,
+    cu[-1] == tokens); a mismatch reports bit 8 of the error word and leaves every output untouched
+    (no tile or output row past the tokens is touched)."""
+    T, H = 100, 2
+    g = gen(31)
+    q = dev(torch.randn(1, T, H, 128, generator=g).bfloat16())
+    k = dev(torch.randn(1, T, H, 128, generator=g).bfloat16())
+    v = dev(torch.randn(1, T, H, 128, generator=g).bfloat16())
+    gg = dev(-torch.rand(1, T, H, generator=g))
+    beta = dev(torch.rand(1, T, H, generator=g).bfloat16())
+    assert _lib.poll_device_error() == 0
+    for cu in ([0, 60, 300], [0, 80, 40, 100], [5, 100]):
+        out = torch.full((1, T, H, 128), 7.0, device="cuda", dtype=torch.bfloat16)
+        fin = torch.full((len(cu) - 1, H, 128, 128), 3.0, device="cuda")
+        ws = torch.empty(ops.delta_rule_workspace_bytes(T, len(cu) - 1, H), device="cuda", dtype=torch.uint8)
+        _lib.call("fdk_chunk_gated_delta_rule_fwd", q.data_ptr(), k.data_ptr(), H * 128, v.data_ptr(), H * 128,
+                  gg.data_ptr(), beta.data_ptr(), dev(torch.tensor(cu, dtype=torch.int32)).data_ptr(), len(cu) - 1,
+                  T, H, 128, 128, 128 ** -0.5, None, out.data_ptr(), fin.data_ptr(), ws.data_ptr(), ws.numel(),
+                  torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert _lib.poll_device_error() == 8, cu
+        assert (out.float() == 7.0).all()
+        assert (fin == 0).all()  # every segment treated as empty: its final state is the (zero) initial state
+    assert _lib.poll_device_error() == 0
+
+
 # --------------------------------------------------------------------------- fused GDN prologue
 def gdn_proj_inputs(lens, H, seed):
     g = gen(seed)

@@ -11,6 +11,8 @@ last and builds all its inputs itself, so it runs the same alone or after the ot
 import pytest
 import torch
 
+from oracle import ops as O
+
 pytestmark = pytest.mark.gpu
 
 if torch.cuda.is_available():
@@ -44,7 +46,9 @@ def _noalloc(q, k, v, gg, beta, cu, init=None):
 
 
 def test_noalloc_matches_workspace_entry_point_on_two_calls():
-    cases = [([1, 64, 65, 170, 3], 16, 1), ([1536], 16, 2)]  # the second fills ~29.5 MiB of scratch
+    # the second call fills ~29.5 MiB of scratch; the third repeats the first, so every tile region
+    # it reads still holds the larger call's stale tiles (nothing in the scratch may start at zero)
+    cases = [([1, 64, 65, 170, 3], 16, 1), ([1536], 16, 2), ([1, 64, 65, 170, 3], 16, 1)]
     for lens, H, seed in cases:
         q, k, v, gg, beta, cu = _inputs(lens, H, seed)
         ref_o, ref_s = ops.chunk_gated_delta_rule(q, k, v, gg, beta, output_final_state=True, cu_seqlens=cu)
@@ -54,6 +58,19 @@ def test_noalloc_matches_workspace_entry_point_on_two_calls():
         assert (got_o.float() - ref_o.float()).abs().max().item() < MAX_ABS
         assert (got_s - ref_s).abs().max().item() < MAX_ABS * max(1.0, ref_s.abs().max().item())
         assert torch.isfinite(got_o.float()).all()
+
+
+def test_noalloc_matches_the_oracle():
+    """The same call against the float32 CPU restatement of the chunked delta rule."""
+    lens, H = [1, 64, 65, 170, 3], 4
+    q, k, v, gg, beta, cu = _inputs(lens, H, 4)
+    got_o, got_s = _noalloc(q, k, v, gg, beta, cu)
+    torch.cuda.synchronize()
+    assert _lib.poll_device_error() == 0
+    ref_o, ref_s = O.chunk_gated_delta_rule(q.cpu(), k.cpu(), v.cpu(), gg.cpu(), beta.cpu().float(),
+                                            output_final_state=True, cu_seqlens=cu.cpu())
+    assert (got_o.float().cpu() - ref_o).abs().max().item() < MAX_ABS
+    assert (got_s.cpu() - ref_s).abs().max().item() < 5e-2 * max(1.0, ref_s.abs().max().item())
 
 
 def test_noalloc_rejects_calls_beyond_its_scratch():
