@@ -47,6 +47,7 @@ __device__ int g_device_error = 0;
 
 struct Params {
   const int32_t* cu;
+  int64_t tokens;  // rows of q / out: stores past them are skipped (cu_seqlens is not checked on the host)
   int hq, hkv;
   float sl2;  // softmax scale * log2(e)
   bf16* out;
@@ -277,7 +278,7 @@ gqa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     if (ok && __all_sync(0xffffffffu, mbar_wait(bar0 + 8 * B_O, 0, abort_flag) ? 1 : 0)) {
       tc_fence_after();
       const int qpos = m0 + row;
-      const bool valid = qpos < L;
+      const bool valid = qpos < L && (int64_t)seg0 + qpos < p.tokens;
       const int h = wg ? hb : ha;
       const float inv_l = 1.0f / l_run;
       const int64_t tok = (int64_t)seg0 + qpos;
@@ -317,6 +318,278 @@ gqa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
   if (tid == 0 && *abort_flag) atomicExch(&g_device_error, 1);
 }
 
+// ---------------------------------------------------------------------------------------------
+// head_dim 256 (the reference op's own shape: native_gqa_kernel.py:132-133 accepts only D = 256,
+// run with 8 query / 2 KV heads).  One CTA = 128 queries of ONE query head: S (128 x 64 fp32) and O
+// (128 x 256 fp32) of two heads would not fit 512 TMEM columns.  KV blocks are 64 keys, so the
+// shared-memory rings fit beside Q: Q [4 boxes][128 rows][128 B] 64 KB, K and V two stages of
+// [4 boxes][64 rows][128 B] (32 KB) each -- 192 KB.  TMEM: S ping-pong [0,64) and [64,128), O
+// [256,512).  Warps 0-3 softmax (thread = query row = TMEM lane), warp 4 TMA producer, warp 5 TMEM
+// allocator + MMA issuer.  The issuer keeps one S block ahead of the softmax:
+//     S(0), S(1); then per block j: [P(j) ready] O += P(j) V(j); S(j+2) into P(j)'s buffer
+// (MMAs of one thread run in issue order, so S(j+2) overwrites P(j) only after the PV reading it),
+// so the tensor core runs PV(j) and S(j+2) while the softmax works on S(j+1).  A lazy O rescale at
+// block j waits for PV(j-1) on its own barrier: S(j)'s commit covers PV(j-2), and PV(j) needs P(j),
+// so that barrier has completed j-1 or j times.
+namespace d256 {
+constexpr int BM = 128, BN = 64, HD = 256;
+constexpr uint32_t QBOX = 128 * 128, KBOX = 64 * 128;  // one swizzle-128B box: rows x 64 bf16
+constexpr uint32_t QT = 4 * QBOX, KT = 4 * KBOX;       // a full 256-wide row block
+constexpr uint32_t OFF_Q = 0, OFF_K0 = QT, OFF_K1 = QT + KT, OFF_V0 = QT + 2 * KT, OFF_V1 = QT + 3 * KT,
+                   OFF_BAR = QT + 4 * KT;
+enum { B_Q = 0, B_KF0, B_KF1, B_KE0, B_KE1, B_VF0, B_VF1, B_VE0, B_VE1, B_S0, B_S1, B_P0, B_P1, B_PV, B_O, NBAR };
+constexpr uint32_t SMEM_BYTES = OFF_BAR + 8 * NBAR + 16 + 1024;
+constexpr int NUM_THREADS = 192;
+constexpr uint32_t TM_S = 0, TM_O = 256, TM_COLS = 512;
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+gqa_fwd_d256_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                    const __grid_constant__ CUtensorMap tv, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t bar0 = base + OFF_BAR;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + OFF_BAR + 8 * NBAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_BAR + 8 * NBAR + 4);
+  auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // grid: x = (segment, query head) with the head fastest, y = query tile from the last one down
+  const int seg = (int)blockIdx.x / p.hq, h = (int)blockIdx.x - seg * p.hq;
+  const int seg0 = p.cu[seg];
+  const int L = p.cu[seg + 1] - seg0;
+  const int mblk = (int)gridDim.y - 1 - (int)blockIdx.y;
+  const int m0 = mblk * BM;
+  if (m0 >= L) return;  // uniform early exit: this tile lies past the segment
+  const int hk = h / (p.hq / p.hkv);
+  const int n_kv = (min(m0 + BM, L) + BN - 1) / BN;  // keys up to the tile's last valid query
+
+  if (tid == 0) {
+    for (int i = 0; i < NBAR; ++i) mbar_init(bar(i), (i == B_P0 || i == B_P1) ? 128u : 1u);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(smem_u32(tmem_slot), TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&tq);
+      prefetch_tmap(&tk);
+      prefetch_tmap(&tv);
+      mbar_expect_tx(bar(B_Q), QT);
+#pragma unroll
+      for (int b = 0; b < 4; ++b) tma_load_2d(base + OFF_Q + b * QBOX, &tq, bar(B_Q), h * HD + 64 * b, seg0 + m0);
+      int issued_k = 0, issued_v = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int ks = j & 1;
+        if (j >= 2 && !mbar_wait(bar(B_KE0 + ks), ((j >> 1) - 1) & 1, abort_flag)) break;
+        const uint32_t kdst = base + (ks ? OFF_K1 : OFF_K0);
+        mbar_expect_tx(bar(B_KF0 + ks), KT);
+#pragma unroll
+        for (int b = 0; b < 4; ++b) tma_load_2d(kdst + b * KBOX, &tk, bar(B_KF0 + ks), hk * HD + 64 * b, seg0 + j * BN);
+        issued_k = j + 1;
+        if (j >= 2 && !mbar_wait(bar(B_VE0 + ks), ((j >> 1) - 1) & 1, abort_flag)) break;
+        const uint32_t vdst = base + (ks ? OFF_V1 : OFF_V0);
+        mbar_expect_tx(bar(B_VF0 + ks), KT);
+#pragma unroll
+        for (int b = 0; b < 4; ++b) tma_load_2d(vdst + b * KBOX, &tv, bar(B_VF0 + ks), hk * HD + 64 * b, seg0 + j * BN);
+        issued_v = j + 1;
+      }
+      // drain: every issued load must have landed before shared memory is released
+      drain(bar(B_Q), 0);
+      for (int j = (issued_k > 2 ? issued_k - 2 : 0); j < issued_k; ++j) drain(bar(B_KF0 + (j & 1)), (j >> 1) & 1);
+      for (int j = (issued_v > 2 ? issued_v - 2 : 0); j < issued_v; ++j) drain(bar(B_VF0 + (j & 1)), (j >> 1) & 1);
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t ID_QK = idesc_bf16(128, BN, false, false);
+      constexpr uint32_t ID_PV = idesc_bf16(128, HD, false, true);  // V is MN-major (d contiguous)
+      const uint64_t dq = sdesc_sw128(base + OFF_Q, 16, 1024);
+      // S(j) = Q K_j^T into S buffer j & 1: K = 256 in 16 steps of 16 (4 per swizzle box)
+      auto issue_s = [&](int j) {
+        const uint64_t dk = sdesc_sw128(base + ((j & 1) ? OFF_K1 : OFF_K0), 16, 1024);
+#pragma unroll
+        for (int kk = 0; kk < 16; ++kk) {
+          const uint32_t qoff = ((kk >> 2) * QBOX + (kk & 3) * 32) >> 4;
+          const uint32_t koff = ((kk >> 2) * KBOX + (kk & 3) * 32) >> 4;
+          umma_ss(tmem + TM_S + 64u * (uint32_t)(j & 1), dq + qoff, dk + koff, ID_QK, kk > 0);
+        }
+        umma_commit(bar(B_S0 + (j & 1)));
+        umma_commit(bar(B_KE0 + (j & 1)));
+      };
+      // O += P(j) V(j): P as bf16 pairs in the first 32 columns of S buffer j & 1; V's four 64-wide
+      // d groups are KBOX apart (lbo), its 8-key atoms 1024 B apart (sbo); K = 64 keys in 4 steps
+      auto issue_pv = [&](int j) {
+        const uint64_t dv = sdesc_sw128(base + ((j & 1) ? OFF_V1 : OFF_V0), KBOX, 1024);
+        const uint32_t tp = tmem + TM_S + 64u * (uint32_t)(j & 1);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_ts(tmem + TM_O, tp + 8 * kk, dv + (uint32_t)(kk * 2048 >> 4), ID_PV, (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(bar(B_PV));
+        umma_commit(bar(B_VE0 + (j & 1)));
+      };
+      bool ok = mbar_wait(bar(B_Q), 0, abort_flag) && mbar_wait(bar(B_KF0), 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0);
+        if (n_kv > 1) {
+          ok = mbar_wait(bar(B_KF1), 0, abort_flag);
+          if (ok) {
+            tc_fence_after();
+            issue_s(1);
+          }
+        }
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        if (!mbar_wait(bar(B_VF0 + (j & 1)), (j >> 1) & 1, abort_flag)) break;
+        if (!mbar_wait(bar(B_P0 + (j & 1)), (j >> 1) & 1, abort_flag)) break;
+        tc_fence_after();
+        issue_pv(j);
+        if (j + 2 < n_kv) {
+          if (!mbar_wait(bar(B_KF0 + (j & 1)), ((j + 2) >> 1) & 1, abort_flag)) break;
+          tc_fence_after();
+          issue_s(j + 2);
+        }
+      }
+      umma_commit(bar(B_O));  // arrives when every MMA above has completed
+      drain(bar(B_O), 0);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax (warps 0-3)
+    const int row = warp * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const uint32_t tO = tmem + lane_base + TM_O;
+    const float sl2 = p.sl2;
+    const int qpos = m0 + row;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const uint32_t tS = tmem + lane_base + TM_S + 64u * (uint32_t)(j & 1);
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(B_S0 + (j & 1)), (j >> 1) & 1, abort_flag) ? 1 : 0)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sr[2][32];
+      tmem_ld32(tS, sr[0]);
+      tmem_ld32(tS + 32, sr[1]);
+      tmem_ld_wait();
+      const int lim = qpos - j * BN;  // key column c is visible when c <= lim
+      if (lim < BN - 1) {             // a block that crosses the diagonal: causal mask
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (c * 32 + i > lim) sr[c][i] = __float_as_uint(-INFINITY);
+      }
+      float mx8[8];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) mx8[a] = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sr[c][i]));
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      const float m_new = fmaxf(m_run, mx * sl2);
+      float alpha = 1.f;
+      bool rescale = false;
+      if (j == 0) {
+        m_run = m_new;
+      } else if (m_new > m_run + 8.0f) {
+        alpha = ex2(m_run - m_new);
+        m_run = m_new;
+        rescale = true;
+      }
+      float sum8[8];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) sum8[a] = 0.f;
+      uint32_t pk[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const float e0 = ex2(fmaf(__uint_as_float(sr[(2 * c) >> 5][(2 * c) & 31]), sl2, -m_run));
+        const float e1 = ex2(fmaf(__uint_as_float(sr[(2 * c + 1) >> 5][(2 * c + 1) & 31]), sl2, -m_run));
+        sum8[(2 * c) & 7] += e0;
+        sum8[(2 * c + 1) & 7] += e1;
+        pk[c] = pack_bf16x2(e0, e1);
+      }
+      tmem_st32(tS, pk);
+      const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+      l_run = l_run * alpha + sum;
+      // O row *= alpha once PV(j-1) has completed (warp-uniform: the TMEM accesses are collective)
+      if (__any_sync(0xffffffffu, rescale)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(bar(B_PV), (j - 1) & 1, abort_flag) ? 1 : 0)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(tO + c * 32, o);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(bar(B_P0 + (j & 1)));
+    }
+    // ------------------------------------------------------------------ epilogue
+    if (ok && __all_sync(0xffffffffu, mbar_wait(bar(B_O), 0, abort_flag) ? 1 : 0)) {
+      tc_fence_after();
+      const bool valid = qpos < L && (int64_t)seg0 + qpos < p.tokens;
+      const float inv_l = 1.0f / l_run;
+      const int64_t tok = (int64_t)seg0 + qpos;
+      bf16* orow = p.out + (tok * p.hq + h) * HD;
+      const bf16* grow = p.gate ? p.gate + tok * p.ld_gate + (int64_t)h * p.gate_hstride : nullptr;
+#pragma unroll 1
+      for (int c = 0; c < 8; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tO + c * 32, o);
+        tmem_ld_wait();
+        if (valid) {
+#pragma unroll
+          for (int v8 = 0; v8 < 4; ++v8) {
+            float y[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) y[i] = __uint_as_float(o[v8 * 8 + i]) * inv_l;
+            if (grow) {
+              float gv[8];
+              unpack8(*reinterpret_cast<const uint4*>(grow + c * 32 + v8 * 8), gv);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) y[i] *= sigmoidf_(gv[i]);
+            }
+            *reinterpret_cast<uint4*>(orow + c * 32 + v8 * 8) = pack8(y);
+          }
+        }
+      }
+    }
+  }
+  // ------------------------------------------------------------------ teardown
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TM_COLS);
+  }
+  if (tid == 0 && *abort_flag) atomicExch(&g_device_error, 1);
+}
+}  // namespace d256
+
 using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
 
 static EncodeFn encode_fn() {
@@ -332,13 +605,13 @@ static EncodeFn encode_fn() {
   return fn;
 }
 
-// 2-D map over [rows, cols] bf16 (row stride ld elements), box 64 x 128, 128-byte swizzle.
-static int make_map(CUtensorMap* m, const void* ptr, int64_t cols, int64_t rows, int64_t ld) {
+// 2-D map over [rows, cols] bf16 (row stride ld elements), box 64 x box_rows, 128-byte swizzle.
+static int make_map(CUtensorMap* m, const void* ptr, int64_t cols, int64_t rows, int64_t ld, int box_rows = 128) {
   EncodeFn enc = encode_fn();
   if (!enc) return set_error(FDK_ERR_DEVICE, "gqa_fwd: cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
-  cuuint32_t box[2] = {64, 128};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -359,9 +632,12 @@ extern "C" int fdk_gqa_fwd(const void* q, int64_t ld_q, const void* k, int64_t l
   using namespace fdk::attn;
   if (int st = check_device()) return st;
   if (!q || !k || !v || !cu_seqlens || !out) return set_error(FDK_ERR_INVALID_ARGUMENT, "gqa_fwd: null pointer");
-  if (head_dim != HD) return set_error(FDK_ERR_UNSUPPORTED, "gqa_fwd: head_dim=%lld (128 supported)", (long long)head_dim);
+  if (head_dim != 128 && head_dim != 256)
+    return set_error(FDK_ERR_UNSUPPORTED, "gqa_fwd: head_dim=%lld (128 and 256 supported)", (long long)head_dim);
+  const int64_t HD = head_dim;
   if (hq <= 0 || hkv <= 0 || hq % hkv) return set_error(FDK_ERR_INVALID_ARGUMENT, "gqa_fwd: hq must be a multiple of hkv");
-  if ((hq / hkv) % 2) return set_error(FDK_ERR_UNSUPPORTED, "gqa_fwd: query heads per KV head must be even");
+  if (HD == 128 && (hq / hkv) % 2)
+    return set_error(FDK_ERR_UNSUPPORTED, "gqa_fwd: with head_dim 128 the query heads per KV head must be even");
   if (num_segments < 1 || num_segments > 65535 || tokens < 0 || max_seqlen < 0)
     return set_error(FDK_ERR_INVALID_ARGUMENT, "gqa_fwd: bad segment count or sizes");
   if (ld_q < hq * HD || ld_k < hkv * HD || ld_v < hkv * HD || (gate && ld_gate < hq * HD))
@@ -370,21 +646,31 @@ extern "C" int fdk_gqa_fwd(const void* q, int64_t ld_q, const void* k, int64_t l
       (gate && (!aligned16(gate) || ld_gate % 8)))
     return set_error(FDK_ERR_ALIGNMENT, "gqa_fwd: pointers and strides must be 16-byte aligned");
   if (tokens == 0 || max_seqlen == 0) return FDK_OK;
+  const int kv_rows = HD == 256 ? d256::BN : BN;
   CUtensorMap mq, mk, mv;
   if (int st = make_map(&mq, q, hq * HD, tokens, ld_q)) return st;
-  if (int st = make_map(&mk, k, hkv * HD, tokens, ld_k)) return st;
-  if (int st = make_map(&mv, v, hkv * HD, tokens, ld_v)) return st;
+  if (int st = make_map(&mk, k, hkv * HD, tokens, ld_k, kv_rows)) return st;
+  if (int st = make_map(&mv, v, hkv * HD, tokens, ld_v, kv_rows)) return st;
   Params prm;
   prm.cu = cu_seqlens;
+  prm.tokens = tokens;
   prm.hq = (int)hq;
   prm.hkv = (int)hkv;
   prm.sl2 = scale * 1.4426950408889634f;
   prm.out = static_cast<bf16*>(out);
   prm.gate = static_cast<const bf16*>(gate);
   prm.ld_gate = ld_gate;
-  prm.gate_hstride = gate_interleaved ? 2 * HD : HD;
-  if (int st = ensure_smem_attr((const void*)gqa_fwd_kernel, (int)SMEM_BYTES, "gqa_fwd")) return st;
+  prm.gate_hstride = (int)(gate_interleaved ? 2 * HD : HD);
   const int64_t mtiles = (max_seqlen + BM - 1) / BM;
+  if (HD == 256) {
+    if (int st = ensure_smem_attr((const void*)d256::gqa_fwd_d256_kernel, (int)d256::SMEM_BYTES, "gqa_fwd")) return st;
+    if (mtiles > 65535 || num_segments * hq > 0x7fffffff)
+      return set_error(FDK_ERR_UNSUPPORTED, "gqa_fwd: too many query tiles or segments");
+    dim3 grid((unsigned)(num_segments * hq), (unsigned)mtiles);
+    d256::gqa_fwd_d256_kernel<<<grid, d256::NUM_THREADS, d256::SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(mq, mk, mv, prm);
+    return check_launch("gqa_fwd (head_dim 256)");
+  }
+  if (int st = ensure_smem_attr((const void*)gqa_fwd_kernel, (int)SMEM_BYTES, "gqa_fwd")) return st;
   if (mtiles > 65535 || num_segments * (hq / 2) > 0x7fffffff)
     return set_error(FDK_ERR_UNSUPPORTED, "gqa_fwd: too many query tiles or segments");
   dim3 grid((unsigned)(num_segments * (hq / 2)), (unsigned)mtiles);

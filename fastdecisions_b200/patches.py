@@ -100,14 +100,20 @@ def install_persistent_residual_rms(core) -> int:
 
 
 # ------------------------------------------------------------------ attention: native GQA
+def _gqa_geometry_supported(self) -> bool:
+    """head_dim 256 (the reference kernel's only shape, native_gqa_kernel.py:132-133) with any head
+    ratio, or head_dim 128 with an even number of query heads per KV head."""
+    ratio = self.config.num_attention_heads // self.config.num_key_value_heads
+    return self.head_dim == 256 or (self.head_dim == 128 and ratio % 2 == 0)
+
+
 def _attn_forward(self, hidden_states, position_embeddings, attention_mask, past_key_values=None, **kwargs):
     """Qwen3_5Attention.forward ([tf]:647-692) with the native GQA kernel (bench_native_gqa_model.py:43-56).
 
     Only plain causal masks are accepted: the reference validates that before its patch
     (bench_native_gqa_model.py:86-98); here a non-None 4-D mask that is not causal falls back."""
     if (past_key_values is not None or self.training or torch.is_grad_enabled() or not hidden_states.is_cuda
-            or hidden_states.dtype != torch.bfloat16 or self.head_dim != 128
-            or (self.config.num_attention_heads // self.config.num_key_value_heads) % 2):
+            or hidden_states.dtype != torch.bfloat16 or not _gqa_geometry_supported(self)):
         return self._gqa_original_forward(hidden_states, position_embeddings, attention_mask,
                                           past_key_values=past_key_values, **kwargs)
     shape = hidden_states.shape[:-1]

@@ -105,8 +105,9 @@ def test_engine_config4_graph(cfg, weights, engine):
 
 def reference_bf16_model(cfg, weights, n_layers=None):
     """The reference's own eager path on this GPU: transformers Qwen3_5TextModel in bf16."""
+    import dataclasses
     from transformers.models.qwen3_5 import modeling_qwen3_5 as mq
-    c = cfg if n_layers is None else W.ModelConfig(num_hidden_layers=n_layers)
+    c = cfg if n_layers is None else dataclasses.replace(cfg, num_hidden_layers=n_layers)
     torch.set_default_dtype(torch.bfloat16)
     try:
         with torch.device("cuda"):
@@ -164,5 +165,32 @@ def test_patched_transformers_model(cfg, weights):
     err_base = (base[0].float().cpu() - ref).abs()
     print(f"patched vs oracle: max {err_ours.max():.4f} mean {err_ours.mean():.5f}; "
           f"unpatched bf16 vs oracle: max {err_base.max():.4f} mean {err_base.mean():.5f}")
+    assert err_ours.mean().item() <= 1.5 * err_base.mean().item() + 1e-3
+    assert err_ours.max().item() <= 2.0 * err_base.max().item() + 2e-2
+
+
+def test_reference_attention_geometry_8q_2kv_d256():
+    """The attention geometry of the reference's real model and kernel (8 query / 2 KV heads of
+    256, native_gqa_kernel.py:132-133; bench_native_gqa_model.py:64-65): the engine end to end
+    against the oracle, and the drop-in patched transformers model against the oracle and the
+    unpatched bf16 path."""
+    from fastdecisions_b200 import patches
+    small = W.ModelConfig(num_hidden_layers=4, num_attention_heads=8, num_key_value_heads=2, head_dim=256,
+                          vocab_size=4096)
+    w = W.synthetic_weights(small)
+    eng = DecisionEngine(small, w, "cuda")
+    reqs = requests(small, ((150, 4), (70, 8), (1, 2), (300, 5)), seed=9)
+    check_decisions(eng.score(reqs), oracle_probs(small, w, reqs))
+    model, _ = reference_bf16_model(small, w)
+    ids = np.random.default_rng(4).integers(0, small.vocab_size, size=(1, 300))
+    x = torch.tensor(ids, device="cuda")
+    with torch.no_grad():
+        base = model(input_ids=x, use_cache=False).last_hidden_state
+    assert patches.install_native_gqa(model) == 1
+    with torch.no_grad():
+        out = model(input_ids=x, use_cache=False).last_hidden_state
+    ref = O.rmsnorm_offset(omodel.forward_hidden(small.as_dict(), w, ids[0]), w["norm.weight"])
+    err_ours = (out[0].float().cpu() - ref).abs()
+    err_base = (base[0].float().cpu() - ref).abs()
     assert err_ours.mean().item() <= 1.5 * err_base.mean().item() + 1e-3
     assert err_ours.max().item() <= 2.0 * err_base.max().item() + 2e-2
