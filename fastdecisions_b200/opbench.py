@@ -10,6 +10,7 @@ device); ``bench.py`` is the end-to-end measurement.
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import math
 import os
@@ -175,8 +176,13 @@ def main(argv=None):
                     help="HBM-bound ops: time CUDA-graph replays of back-to-back calls over enough "
                          "independent buffer sets to move this many MB per pass (e.g. 1024, far above the "
                          "126 MB L2) instead of single calls with an L2 flush between them")
+    ap.add_argument("--attn", default=None,
+                    help="attention geometry hq,hkv,head_dim (e.g. 8,2,256: the reference kernel's own shape)")
     args = ap.parse_args(argv)
     cfg = ModelConfig()
+    if args.attn:
+        hq, hkv, d = (int(x) for x in args.attn.split(","))
+        cfg = dataclasses.replace(cfg, num_attention_heads=hq, num_key_value_heads=hkv, head_dim=d)
     lens = [int(x) for x in args.lens.split(",")] if args.lens else batch_lengths(args.batch)
     peaks = _peaks()
     for op in (OPS if args.op == "all" else (args.op,)):
@@ -191,6 +197,7 @@ def main(argv=None):
             ms = time_op(fn, args.iters, args.warmup)
         achieved = work / (ms * 1e-3) / (1e12 if bound == "tensor" else 1e9)
         print(json.dumps({"op": op, "batch": "lens" if args.lens else args.batch, "tokens": int(sum(lens)),
+                          "attn": [cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim],
                           "segments": len(lens),
                           "max_len": int(max(lens)), "us": round(ms * 1e3, 2), "bound": bound,
                           "achieved": round(achieved, 1), "unit": "TFLOP/s" if bound == "tensor" else "GB/s",
