@@ -759,9 +759,16 @@ struct RParams {
 struct StageMeta {  // written by the producer before the stage's expect_tx arrive
   int s, h, c, nch;
   float gamma;
-  int pad[3];
+  int half;  // SPLIT == 2: which 64 dv rows of the head this chain carries
+  int pad[2];
 };
 
+// SPLIT == 1: a chain is one (segment, head); the state S^T is 128 dv rows (M = 128 MMAs).
+// SPLIT == 2: every dv row of S^T evolves on its own (v_new, o and the update of row r read only
+// row r of S^T, U^T and vn), so a (segment, head) is run as two chains of 64 dv rows each on two
+// CTAs: twice the chains when there are fewer chains than SMs (batch 1 has 16), with M = 64 MMAs
+// (accumulator rows in lanes 0-15 of each TMEM lane quarter) and only that half of U^T loaded.
+template <int SPLIT>
 __global__ void __launch_bounds__(THREADS, 1)
 delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_constant__ CUtensorMap mqg,
                       const __grid_constant__ CUtensorMap mkg, const __grid_constant__ CUtensorMap ma,
@@ -799,7 +806,8 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
       prefetch_tmap(&mkg);
       prefetch_tmap(&ma);
       prefetch_tmap(&mut);
-      const int items = p.nseg * H;
+      const int items = p.nseg * H * SPLIT;
+      constexpr uint32_t stage_tx = SPLIT == 1 ? ST_BYTES : ST_BYTES - KM_HALF;  // U^T: 128 or 64 dv rows
       int n = 0;  // real chunks pushed into the ring by this CTA
       bool closed = false;
       while (true) {
@@ -812,7 +820,7 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
           closed = true;
           break;
         }
-        const int s = item / H, h = item - s * H;
+        const int s = item / (H * SPLIT), rem = item - s * (H * SPLIT), h = rem / SPLIT, half = rem - h * SPLIT;
         const int c0 = __ldg(p.table + s), nch = __ldg(p.table + s + 1) - c0;
         bool ok = true;
         for (int c = 0; c < nch; ++c, ++n) {
@@ -823,17 +831,18 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
           meta[st].h = h;
           meta[st].c = c;
           meta[st].nch = nch;
+          meta[st].half = half;
           meta[st].gamma = __ldg(reinterpret_cast<const float*>(p.tiles + (size_t)z * CH_BYTES + OFF_GAMMA));
           const uint32_t sb = base + st * ST_BYTES;
           const uint32_t fb = bar0 + 8 * (B_FULL0 + st);
-          mbar_expect_tx(fb, ST_BYTES);
+          mbar_expect_tx(fb, stage_tx);
           tma_load_3d(sb + ST_W, &mw, fb, 0, 0, z);
           tma_load_3d(sb + ST_QG, &mqg, fb, 0, 0, z);
           tma_load_3d(sb + ST_QG + KM_HALF, &mqg, fb, 64, 0, z);
           tma_load_3d(sb + ST_KG, &mkg, fb, 0, 0, z);
           tma_load_3d(sb + ST_KG + KM_HALF, &mkg, fb, 64, 0, z);
           tma_load_3d(sb + ST_A, &ma, fb, 0, 0, z);
-          tma_load_3d(sb + ST_UT, &mut, fb, 0, 0, z);
+          tma_load_3d(sb + ST_UT, &mut, fb, 0, 64 * half, z);  // SPLIT == 2: the map's box is 64 rows
         }
         if (!ok) break;
       }
@@ -848,9 +857,11 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t ID_N64 = idesc_bf16(128, 64, false, false);
-      constexpr uint32_t ID_N64_BMN = idesc_bf16(128, 64, false, true);
-      constexpr uint32_t ID_N128_BMN = idesc_bf16(128, 128, false, true);
+      constexpr int MR = 128 / SPLIT;  // dv rows of the chain: the MMAs' M
+      constexpr uint32_t A_KHALF = (uint32_t)MR * 128u;  // bytes of one 64-wide dk half of the S^T A tile
+      constexpr uint32_t ID_N64 = idesc_bf16(MR, 64, false, false);
+      constexpr uint32_t ID_N64_BMN = idesc_bf16(MR, 64, false, true);
+      constexpr uint32_t ID_N128_BMN = idesc_bf16(MR, 128, false, true);
       const uint64_t dSA = sdesc_sw128(base + OFF_SA, 16, 1024), dVA = sdesc_sw128(base + OFF_VA, 16, 1024);
       for (int n = 0;; ++n) {
         const int st = n & 1;
@@ -867,14 +878,14 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
         // vn = S^T W^T  (K = 128 dk: 2 swizzle halves x 4 steps of 16; W^T [dk][tok] is MN-major)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t aoff = (uint32_t)(kk >> 2) * (128u * 128u) + (uint32_t)(kk & 3) * 32u;
+          const uint32_t aoff = (uint32_t)(kk >> 2) * A_KHALF + (uint32_t)(kk & 3) * 32u;
           umma_ss(tmem + TM_VN, dSA + (aoff >> 4), dW + ((uint32_t)kk * 2048u >> 4), ID_N64_BMN, kk > 0 ? 1u : 0u);
         }
         umma_commit(bar0 + 8 * B_VN);
         // o^T = S^T Qg^T
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t aoff = (uint32_t)(kk >> 2) * (128u * 128u) + (uint32_t)(kk & 3) * 32u;
+          const uint32_t aoff = (uint32_t)(kk >> 2) * A_KHALF + (uint32_t)(kk & 3) * 32u;
           const uint32_t boff = (uint32_t)(kk >> 2) * KM_HALF + (uint32_t)(kk & 3) * 32u;
           umma_ss(tO, dSA + (aoff >> 4), dQG + (boff >> 4), ID_N64, kk > 0 ? 1u : 0u);
         }
@@ -901,95 +912,127 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
     // ---------------------------------------------------------------- state warps (256 threads)
     // Two warps per TMEM lane quarter; warp half `hf` owns half of every row's columns: S^T
     // columns [64 hf, +64), vn / o columns (tokens) [32 hf, +32).
+    // SPLIT == 1: thread = dv row (TMEM lane) and all of its warp half's columns.
+    // SPLIT == 2: thread = chain row 16 q4 + (lane & 15) (TMEM lanes 0-15 of the quarter, the M = 64
+    //   accumulator layout) and column part sub = lane >> 4 of its warp half's columns: S^T
+    //   columns [64 hf + 32 sub, +32), vn / o columns [32 hf + 16 sub, +16) (16x32bx2 accesses).
+    constexpr int MR = 128 / SPLIT;   // dv rows of a chain
     const int q4 = warp & 3;          // the TMEM lane quarter this warp may access
     const int hf = (warp - 2) >> 2;   // 0 for warps 2-5, 1 for warps 6-9
-    const int r = q4 * 32 + lane;     // dv row == TMEM lane
+    const int sub = SPLIT == 2 ? lane >> 4 : 0;
+    const int r = SPLIT == 1 ? q4 * 32 + lane : q4 * 16 + (lane & 15);  // row of the chain's S^T
     const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
     const uint32_t tS = tmem + lane_addr + TM_S + 64 * hf, tVN = tmem + lane_addr + TM_VN + 32 * hf,
                    tO = tmem + lane_addr + TM_O + 32 * hf;
     uint8_t* sa = gbase + OFF_SA;
     uint8_t* va = gbase + OFF_VA;
-    bf16* ost = reinterpret_cast<bf16*>(gbase + OFF_OST) + (hf * 4 + q4) * (32 * 32);  // [32 tok][32 dv]
+    // o staging per state warp: [32 tok][32 dv] (SPLIT 1) or [32 tok][16 dv] (SPLIT 2) bf16
+    bf16* ost = reinterpret_cast<bf16*>(gbase + OFF_OST) + (hf * 4 + q4) * (32 * 32);
+    constexpr int NCB = SPLIT == 1 ? 2 : 1;  // 32-column S^T pieces per thread
+    auto scol = [&](int cb) { return 64 * hf + 32 * (SPLIT == 1 ? cb : sub); };  // first dk column of piece cb
+    auto s_ld = [&](int cb, uint32_t (&v)[32]) {
+      if constexpr (SPLIT == 1) tmem_ld32(tS + cb * 32, v); else tmem_ld16x2_x32(tS, v);
+    };
+    auto s_st = [&](int cb, const uint32_t (&v)[32]) {
+      if constexpr (SPLIT == 1) tmem_st32(tS + cb * 32, v); else tmem_st16x2_x32(tS, v);
+    };
 
-    // o^T of chunk (s, h, c) (complete in TMEM buffer b) -> out[token][h][dv], 64-byte pieces
-    auto o_epilogue = [&](int b, int s, int h, int c) {
-      uint32_t o[32];
-      tmem_ld32(tO + 64 * b, o);
-      tmem_ld_wait();
-#pragma unroll
-      for (int t = 0; t < 32; ++t) ost[t * 32 + lane] = __float2bfloat16_rn(__uint_as_float(o[t]));
-      __syncwarp();
+    // o^T of chunk (s, h, c) (complete in TMEM buffer b) -> out[token][h][dv]
+    auto o_epilogue = [&](int b, int s, int h, int c, int half) {
       const int tok0 = p.cu[s] + c * DR_C + 32 * hf;
       const int len = min(32, p.cu[s + 1] - tok0);
+      if constexpr (SPLIT == 1) {
+        uint32_t o[32];
+        tmem_ld32(tO + 64 * b, o);
+        tmem_ld_wait();
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int e = lane + i * 32, tr = e >> 2, ch = e & 3;
-        if (tr < len)
-          *reinterpret_cast<uint4*>(p.out + ((int64_t)(tok0 + tr) * H + h) * DR_D + q4 * 32 + ch * 8) =
-              *reinterpret_cast<const uint4*>(ost + tr * 32 + ch * 8);
+        for (int t = 0; t < 32; ++t) ost[t * 32 + lane] = __float2bfloat16_rn(__uint_as_float(o[t]));
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {  // 64-byte pieces
+          const int e = lane + i * 32, tr = e >> 2, ch = e & 3;
+          if (tr < len)
+            *reinterpret_cast<uint4*>(p.out + ((int64_t)(tok0 + tr) * H + h) * DR_D + q4 * 32 + ch * 8) =
+                *reinterpret_cast<const uint4*>(ost + tr * 32 + ch * 8);
+        }
+      } else {
+        uint32_t o[16];
+        tmem_ld16x2_x16(tO + 64 * b, o);
+        tmem_ld_wait();
+#pragma unroll
+        for (int t = 0; t < 16; ++t) ost[(16 * sub + t) * 16 + (lane & 15)] = __float2bfloat16_rn(__uint_as_float(o[t]));
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {  // 32-byte pieces
+          const int e = lane + i * 32, tr = e >> 1, ch = e & 1;
+          if (tr < len)
+            *reinterpret_cast<uint4*>(p.out + ((int64_t)(tok0 + tr) * H + h) * DR_D + 64 * half + q4 * 16 + ch * 8) =
+                *reinterpret_cast<const uint4*>(ost + tr * 16 + ch * 8);
+        }
       }
       __syncwarp();
     };
-    auto write_final = [&](int s, int h) {
+    // final_state[s][h][dk][dv] = S^T[dv][dk]; dv = MR * half + r
+    auto write_final = [&](int s, int h, int half) {
       if (!p.final_state) return;
       const int64_t sh = (int64_t)s * H + h;
 #pragma unroll
-      for (int cb = 0; cb < 2; ++cb) {
+      for (int cb = 0; cb < NCB; ++cb) {
         uint32_t v[32];
-        tmem_ld32(tS + cb * 32, v);
+        s_ld(cb, v);
         tmem_ld_wait();
 #pragma unroll
         for (int i = 0; i < 32; ++i)
-          p.final_state[(sh * DR_D + 64 * hf + cb * 32 + i) * DR_D + r] = __uint_as_float(v[i]);
+          p.final_state[(sh * DR_D + scol(cb) + i) * DR_D + MR * half + r] = __uint_as_float(v[i]);
       }
     };
 
-    int ps = -1, ph = 0, pc = 0;  // the previous chunk (its output is written one chunk late)
+    int ps = -1, ph = 0, pc = 0, phalf = 0;  // the previous chunk (its output is written one chunk late)
     for (int n = 0;; ++n) {
       const int st = n & 1;
       if (!warp_wait(bar0 + 8 * (B_FULL0 + st), (n >> 1) & 1, abort_flag)) break;
-      const int s = meta[st].s, h = meta[st].h, c = meta[st].c;
+      const int s = meta[st].s, h = meta[st].h, c = meta[st].c, half = SPLIT == 1 ? 0 : meta[st].half;
       const float gam = meta[st].gamma;
       if (n > 0) {  // S^T of the previous chunk is complete
         if (!warp_wait(bar0 + 8 * B_SDONE, (n - 1) & 1, abort_flag)) break;
         tc_fence_after();
       }
       if (s < 0 || c == 0) {  // chain boundary
-        if (ps >= 0) write_final(ps, ph);
+        if (ps >= 0) write_final(ps, ph, phalf);
         if (s < 0) {  // closing stage: output of the last chunk, then done
           if (ps >= 0 && warp_wait(bar0 + 8 * (B_ODONE0 + (st ^ 1)), ((n - 1) >> 1) & 1, abort_flag)) {
             tc_fence_after();
-            o_epilogue(st ^ 1, ps, ph, pc);
+            o_epilogue(st ^ 1, ps, ph, pc, phalf);
           }
           break;
         }
         const int64_t sh = (int64_t)s * H + h;
 #pragma unroll
-        for (int cb = 0; cb < 2; ++cb) {  // S^T[r][dk] = initial_state[dk][r]
+        for (int cb = 0; cb < NCB; ++cb) {  // S^T[r][dk] = initial_state[dk][MR * half + r]
           uint32_t v[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i)
-            v[i] = __float_as_uint(p.init_state ? p.init_state[(sh * DR_D + 64 * hf + cb * 32 + i) * DR_D + r] : 0.f);
-          tmem_st32(tS + cb * 32, v);
+            v[i] = __float_as_uint(p.init_state ? p.init_state[(sh * DR_D + scol(cb) + i) * DR_D + MR * half + r] : 0.f);
+          s_st(cb, v);
         }
         tmem_st_wait();
       }
       // S^T -> bf16 A tile; S^T *= gamma in TMEM (this chunk's MMAs read the A tile)
 #pragma unroll
-      for (int cb = 0; cb < 2; ++cb) {
+      for (int cb = 0; cb < NCB; ++cb) {
         uint32_t v[32];
-        tmem_ld32(tS + cb * 32, v);
+        s_ld(cb, v);
         tmem_ld_wait();
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           float f[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(v[j * 8 + i]);
-          *reinterpret_cast<uint4*>(sa + sw128_off(r, hf * 8 + cb * 4 + j, 128)) = pack8(f);
+          *reinterpret_cast<uint4*>(sa + sw128_off(r, scol(cb) / 8 + j, MR)) = pack8(f);
         }
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * gam);
-        tmem_st32(tS + cb * 32, v);
+        s_st(cb, v);
       }
       tmem_st_wait();
       fence_proxy_async_smem();
@@ -999,17 +1042,26 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
       if (!warp_wait(bar0 + 8 * B_VN, n & 1, abort_flag)) break;
       tc_fence_after();
       {
-        const uint8_t* ut = gbase + st * ST_BYTES + ST_UT;
+        const uint8_t* ut = gbase + st * ST_BYTES + ST_UT;  // the chain's MR rows of U^T
+        constexpr int NV = 32 / SPLIT;                     // vn columns per thread
         uint32_t v[32];
-        tmem_ld32(tVN, v);
-        tmem_ld_wait();
+        if constexpr (SPLIT == 1) {
+          tmem_ld32(tVN, v);
+        } else {
+          uint32_t w[16];
+          tmem_ld16x2_x16(tVN, w);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+          for (int i = 0; i < 16; ++i) v[i] = w[i];
+        }
+        tmem_ld_wait();
+        const int c16_0 = (32 * hf + 16 * sub) / 8;
+#pragma unroll
+        for (int j = 0; j < NV / 8; ++j) {
           float u[8], f[8];
-          unpack8(*reinterpret_cast<const uint4*>(ut + sw128_off(r, hf * 4 + j, 128)), u);
+          unpack8(*reinterpret_cast<const uint4*>(ut + sw128_off(r, c16_0 + j, MR)), u);
 #pragma unroll
           for (int i = 0; i < 8; ++i) f[i] = u[i] - __uint_as_float(v[j * 8 + i]);
-          *reinterpret_cast<uint4*>(va + sw128_off(r, hf * 4 + j, 128)) = pack8(f);
+          *reinterpret_cast<uint4*>(va + sw128_off(r, c16_0 + j, MR)) = pack8(f);
         }
       }
       fence_proxy_async_smem();
@@ -1019,11 +1071,12 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
       if (ps >= 0) {
         if (!warp_wait(bar0 + 8 * (B_ODONE0 + (st ^ 1)), ((n - 1) >> 1) & 1, abort_flag)) break;
         tc_fence_after();
-        o_epilogue(st ^ 1, ps, ph, pc);
+        o_epilogue(st ^ 1, ps, ph, pc, phalf);
       }
       ps = s;
       ph = h;
       pc = c;
+      phalf = half;
     }
   }
   __syncwarp();
@@ -1064,13 +1117,14 @@ static EncodeFn encode_fn() {
 }
 
 // 3-D map over one operand of every workspace tile: [n_tiles][rows][cols] bf16, tile stride
-// CH_BYTES, box 64 x rows x 1, 128-byte swizzle.
-static int tile_map(CUtensorMap* m, const uint8_t* tiles, size_t off, int cols, int rows, int64_t n_tiles) {
+// CH_BYTES, box 64 x box_rows x 1 (box_rows = rows unless given), 128-byte swizzle.
+static int tile_map(CUtensorMap* m, const uint8_t* tiles, size_t off, int cols, int rows, int64_t n_tiles,
+                    int box_rows = 0) {
   EncodeFn enc = encode_fn();
   if (!enc) return set_error(FDK_ERR_DEVICE, "chunk_gated_delta_rule: cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)n_tiles};
   cuuint64_t strides[2] = {(cuuint64_t)cols * 2, (cuuint64_t)CH_BYTES};
-  cuuint32_t box[3] = {64, (cuuint32_t)rows, 1};
+  cuuint32_t box[3] = {64, (cuuint32_t)(box_rows ? box_rows : rows), 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<uint8_t*>(tiles + off), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1141,13 +1195,20 @@ static int launch_recur(int nseg, int heads, int64_t n_tiles, cudaStream_t s, co
   if (int st = tile_map(&mqg, tiles, OFF_QG, DR_D, DR_C, n_tiles)) return st;
   if (int st = tile_map(&mkg, tiles, OFF_KG, DR_D, DR_C, n_tiles)) return st;
   if (int st = tile_map(&ma, tiles, OFF_A, DR_C, DR_C, n_tiles)) return st;
-  if (int st = tile_map(&mut, tiles, OFF_UT, DR_C, DR_D, n_tiles)) return st;
+  // Fewer (segment, head) chains than half the SMs (batch-1 decisions: 16): run each as two chains
+  // of 64 dv rows on two CTAs; otherwise every SM already has a whole chain to run.
+  const int64_t chains = (int64_t)nseg * heads;
+  const bool split = 2 * chains <= sm_count();
+  if (int st = tile_map(&mut, tiles, OFF_UT, DR_C, DR_D, n_tiles, split ? DR_D / 2 : DR_D)) return st;
   const RParams prm{cu, table, counter, nseg, heads, tiles, init, out, fin};
-  if (int st = ensure_smem_attr((const void*)delta_recur_tc_kernel, (int)SMEM_BYTES, "chunk_gated_delta_rule/recurrence"))
-    return st;
-  const int64_t items = (int64_t)nseg * heads;
+  const void* fn = split ? (const void*)delta_recur_tc_kernel<2> : (const void*)delta_recur_tc_kernel<1>;
+  if (int st = ensure_smem_attr(fn, (int)SMEM_BYTES, "chunk_gated_delta_rule/recurrence")) return st;
+  const int64_t items = chains * (split ? 2 : 1);
   const unsigned grid = (unsigned)(items < sm_count() ? items : sm_count());
-  delta_recur_tc_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(mw, mqg, mkg, ma, mut, prm);
+  if (split)
+    delta_recur_tc_kernel<2><<<grid, THREADS, SMEM_BYTES, s>>>(mw, mqg, mkg, ma, mut, prm);
+  else
+    delta_recur_tc_kernel<1><<<grid, THREADS, SMEM_BYTES, s>>>(mw, mqg, mkg, ma, mut, prm);
   return check_launch("chunk_gated_delta_rule/recurrence");
 }
 

@@ -305,6 +305,14 @@ def test_delta_rule_long_segment_many_heads():
     delta_check(2600, 8, 9, cu=[0, 2560, 2600], init=True)
 
 
+def test_delta_rule_many_chains_whole_chain_path():
+    # 10 segments x 8 heads = 80 (segment, head) chains, more than half of the 148 SMs: each chain
+    # runs whole on one CTA (M = 128); the tests above, with few chains, run every chain as two
+    # 64-row halves on two CTAs (M = 64)
+    lens = [100, 1, 64, 65, 130, 7, 200, 63, 128, 50]
+    delta_check(sum(lens), 8, 10, cu=[0] + list(torch.tensor(lens).cumsum(0).tolist()), init=True)
+
+
 def test_delta_rule_golden(golden):
     f = golden["delta_d128"]
     o, st = ops.chunk_gated_delta_rule(dev(f["q"].bfloat16()), dev(f["k"].bfloat16()), dev(f["v"].bfloat16()),
