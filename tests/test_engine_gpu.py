@@ -6,11 +6,11 @@ bound however exact each layer is:
 * per layer, in isolation (each layer gets the oracle's own residual stream as input): the layer's
   contribution matches the float32 oracle within max-abs 2e-2 relative to its magnitude -- the
   north star's "layer outputs" bound;
-* end to end, over 24 layers of a random-weight model whose output distribution is close to flat:
-  every bf16 forward, including exact CPU emulations of bf16 storage and the reference's own
-  transformers bf16 path, drifts ~2-3 pp from float32, so the bound there is 3 pp, identical
-  argmax on every decision whose float32 top-1 margin is at least 5 pp, and no worse than the
-  reference's own bf16 eager path on the same requests.
+* end to end, over 24 layers: bf16 storage of activations alone (measured by rounding the float32
+  reference at the same storage points) moves the answer probabilities by ~1 pp on average (up to
+  ~3 pp) on this random-weight model, so the bounds there are: no worse than the reference's own
+  bf16 GPU path on the same requests, no more drift than bf16 storage alone produces, identical
+  argmax on every decision whose float32 top-1 margin is at least 5 pp.
 """
 import numpy as np
 import pytest
@@ -66,8 +66,10 @@ def check_decisions(got, want, bound=0.03, margin=0.05):
     return dp
 
 
-def test_layer_outputs_isolated(cfg, weights, engine):
-    reqs = requests(cfg, ((200, 4), (1, 2), (130, 8)), seed=11)
+@pytest.mark.parametrize("case", ["config4", "varlen"])
+def test_layer_outputs_isolated(cfg, weights, engine, case):
+    # the 1536-token config-4 request, and three packed segments (200, 1, 130 tokens)
+    reqs = [W.config4_request()] if case == "config4" else requests(cfg, ((200, 4), (1, 2), (130, 8)), seed=11)
     b = pack(reqs)
     cu_h = torch.tensor(b.cu_seqlens)
     (ids, cu, pos, slots, nopts), _ = engine.to_device(b)
@@ -125,23 +127,41 @@ def reference_bf16_model(cfg, weights, n_layers=None):
 
 
 def test_no_worse_than_reference_bf16_path(cfg, weights, engine):
-    reqs = requests(cfg, ((70, 2), (150, 8), (33, 4), (400, 5), (777, 8), (256, 4)), seed=3)
-    want = oracle_probs(cfg, weights, reqs)
+    """32 config-5 requests (lengths 64-6068), anchored on the reference's own float32 forward
+    (transformers Qwen3_5TextModel with its torch paths, TF32 off, on this GPU):
+    * our mean |dp| is at most the reference bf16 GPU path's (+ 0.1 pp) and we get at least as many
+      argmax decisions right;
+    * our drift is what bf16 storage alone produces: the float32 reference with bf16 rounding at
+      the same storage points as this engine (linear-layer inputs and outputs, the token mixers'
+      q / k / v / outputs) drifts as much (x 1.1 + 0.05 pp), so the kernels add no error of their own;
+    * no decision with a float32 top-1 margin of >= 5 pp changes."""
+    from fastdecisions_b200 import paritybench as PB
+    reqs = W.config5_requests(256)[:32]
+    letters = W.letter_weight(weights).float().cuda()
+    flags = (torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32)
+    torch.backends.cuda.matmul.allow_tf32 = torch.backends.cudnn.allow_tf32 = False
+    try:
+        ref32 = PB.reference_model(cfg, weights, torch.float32, "cuda", fast_paths=False)
+        want = PB.reference_probs(ref32, reqs, letters, "cuda")
+        with PB.rounding(ref32, {"linear_in", "linear_out", "mixer"}):
+            storage = PB.reference_probs(ref32, reqs, letters, "cuda")
+        del ref32
+    finally:
+        torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = flags
     ours = engine.score(reqs)
-    model, _ = reference_bf16_model(cfg, weights)
-    lw = W.letter_weight(weights).float().cuda()
-    ref = []
-    with torch.no_grad():
-        for r in reqs:
-            hs = model(input_ids=torch.tensor(r.ids[None].astype(np.int64), device="cuda"), use_cache=False).last_hidden_state
-            lg = (hs[0, r.slot].float() @ lw.t()).masked_fill(torch.arange(8, device="cuda") >= r.nopts, float("-inf"))
-            ref.append(torch.softmax(lg, -1).cpu().numpy())
-    ref = np.stack(ref)
-    ours_dev = np.abs(ours - want).max(1)
-    ref_dev = np.abs(ref - want).max(1)
-    print("max |dp| per request, ours:", np.round(ours_dev * 100, 2), " reference bf16:", np.round(ref_dev * 100, 2))
-    assert ours_dev.mean() <= 2.0 * ref_dev.mean() + 0.005
-    assert (ours.argmax(1) == want.argmax(1)).sum() >= (ref.argmax(1) == want.argmax(1)).sum() - 1
+    ref16 = PB.reference_model(cfg, weights, torch.bfloat16, "cuda", fast_paths=True)
+    ref = PB.reference_probs(ref16, reqs, letters, "cuda")
+    del ref16
+    torch.cuda.empty_cache()
+    s_ours, s_ref, s_sto = (PB.summarize(p, want) for p in (ours, ref, storage))
+    print(f"mean |dp| pp: ours {s_ours['mean_dp_pp']}, reference bf16 {s_ref['mean_dp_pp']}, "
+          f"bf16 storage alone {s_sto['mean_dp_pp']}; argmax ours {s_ours['argmax_agree']}/32, "
+          f"reference bf16 {s_ref['argmax_agree']}/32")
+    assert s_ours["mean_dp_pp"] <= s_ref["mean_dp_pp"] + 0.1
+    assert s_ours["argmax_agree"] >= s_ref["argmax_agree"]
+    assert s_ours["mean_dp_pp"] <= 1.1 * s_sto["mean_dp_pp"] + 0.05
+    assert s_ours["flips_on_clear"] == 0
+    check_decisions(ours, want, bound=0.05)
 
 
 def test_patched_transformers_model(cfg, weights):
