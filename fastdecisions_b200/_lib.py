@@ -42,6 +42,7 @@ SIGNATURES = {
     "fdk_poll_device_error": (i32, [C.POINTER(C.c_int)]),
     "fdk_selftest_bounded_wait": (i32, [i64, vp]),
     "fdk_embed": (i32, [vp, vp, i64, i64, vp, i64, vp]),
+    "fdk_gemm_bf16": (i32, [vp, i64, vp, i64, vp, i64, i64, i64, i64, i32, vp]),
     "fdk_swiglu": (i32, [vp, i64, vp, i64, i64, vp]),
     "fdk_slot_readout": (i32, [vp, i32, vp, i64, vp, vp, i64, vp, i32, vp, i64, f32, f32, vp, vp, vp]),
 }

@@ -719,6 +719,9 @@ extern "C" int fdk_poll_device_error(int* code) {
   const int d = fdk::delta_take_device_error();
   if (d < 0) return set_error(FDK_ERR_DEVICE, "poll_device_error: cannot read the device error word");
   h |= ((d & 1) << 1) | ((d & 2) << 2);  // 2: a delta-rule wait ran out; 8: cu_seqlens rejected
+  const int gm = fdk::gemm_take_device_error();
+  if (gm < 0) return set_error(FDK_ERR_DEVICE, "poll_device_error: cannot read the device error word");
+  if (gm) h |= 16;  // a GEMM wait ran out
   if (code) *code = h;
   return FDK_OK;
 }

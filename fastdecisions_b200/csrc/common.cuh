@@ -24,6 +24,8 @@ int sm_count();
 int ensure_smem_attr(const void* func, int bytes, const char* what);
 // Reads and clears the delta-rule recurrence's device error word (set when a bounded wait ran out).
 int delta_take_device_error();
+// Reads and clears the GEMM kernel's device error word.
+int gemm_take_device_error();
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

@@ -30,8 +30,9 @@ __device__ __forceinline__ int64_t next_start(const int32_t* cu, int nseg, int64
   return cu[lo];
 }
 
-// Shared-memory staged kernel: a CTA owns a 128-channel column block and CONV_TILES_PER_CTA
-// consecutive 64-token tiles.  Tile rows [t0 - 3, t0 + 64) (the 3-row causal halo included) stream
+// Shared-memory staged kernel: a CTA owns a 128-channel column block and `tpc` (1-4) consecutive
+// 64-token tiles -- as many as keep every SM's six CTA slots busy in one wave (small inputs such
+// as one 2048-token request get one or two tiles a CTA, so more loads are in flight at once).  Tile rows [t0 - 3, t0 + 64) (the 3-row causal halo included) stream
 // into shared memory with cp.async, double-buffered, so the next tile's 16-byte loads are in flight
 // while the current one is convolved.  Thread (cq, rg) computes 8 channels x 8 rows with the taps
 // in registers (16-byte shared loads and global stores); a half-warp stores 256 contiguous bytes
@@ -39,7 +40,9 @@ __device__ __forceinline__ int64_t next_start(const int32_t* cu, int nseg, int64
 constexpr int CONV_CB = 128;            // channels per CTA
 constexpr int CONV_ROWS = 64;           // tokens per tile
 constexpr int CONV_HALO = 3;
-constexpr int CONV_TILES_PER_CTA = 4;
+constexpr int CONV_MAX_TILES_PER_CTA = 4;
+constexpr int CONV_CTAS_PER_SM = 6;
+constexpr int64_t CONV_DIRECT_MAX_TOKENS = 8192;  // up to this many tokens the direct kernel runs
 constexpr int CONV_SROWS = CONV_ROWS + CONV_HALO;
 constexpr int CONV_RPT = 8;             // rows per thread
 
@@ -47,16 +50,16 @@ template <int KW>
 __global__ void __launch_bounds__(CONV_THREADS, 6) packed_conv_silu_smem_kernel(
     const bf16* __restrict__ x, int64_t ldx, const bf16* __restrict__ w, int64_t ntok, int64_t period,
     const int32_t* __restrict__ cu, int nseg, int channels, int key_dim, bf16* __restrict__ q,
-    bf16* __restrict__ k, bf16* __restrict__ v) {
+    bf16* __restrict__ k, bf16* __restrict__ v, int tpc) {
   __shared__ __align__(16) bf16 tile[2][CONV_SROWS][CONV_CB];
   __shared__ long long seg_info[CONV_ROWS / CONV_RPT][2];  // per row group: segment start, next start
   const int tid = threadIdx.x;
   const int cb0 = blockIdx.x * CONV_CB;
   const int cq = tid & 15, rg = tid >> 4;   // 8 channels, 8 rows
   const int c0 = cb0 + cq * 8;
-  const int64_t first = (int64_t)blockIdx.y * CONV_TILES_PER_CTA;
+  const int64_t first = (int64_t)blockIdx.y * tpc;
   const int64_t ntiles = (ntok + CONV_ROWS - 1) / CONV_ROWS;
-  const int64_t last = (first + CONV_TILES_PER_CTA < ntiles) ? first + CONV_TILES_PER_CTA : ntiles;
+  const int64_t last = (first + tpc < ntiles) ? first + tpc : ntiles;
   if (first >= last) return;
 
   auto issue = [&](int64_t ti, int b) {
@@ -163,6 +166,85 @@ __global__ void __launch_bounds__(CONV_THREADS, 6) packed_conv_silu_smem_kernel(
   }
 }
 
+// Direct kernel for small inputs (a few thousand tokens: the staged kernel cannot fill the SMs'
+// load pipes there).  Thread = 8 channels x 8 consecutive tokens; a warp covers 256 contiguous
+// channels of one row group, a CTA four row groups.  All 11 rows a thread needs (the 3-row causal
+// halo included; halo rows are L2 hits) are loaded with independent 16-byte loads before any
+// arithmetic, so every thread has its whole input in flight at once.  Channel pairs use the packed
+// fp32 pipe (fma.rn.f32x2): the same roundings per lane as the scalar chain of the staged kernel.
+template <int KW>
+__global__ void __launch_bounds__(128) packed_conv_silu_direct_kernel(
+    const bf16* __restrict__ x, int64_t ldx, const bf16* __restrict__ w, int64_t ntok, int64_t period,
+    const int32_t* __restrict__ cu, int nseg, int channels, int key_dim, bf16* __restrict__ q,
+    bf16* __restrict__ k, bf16* __restrict__ v) {
+  const int lane = threadIdx.x & 31, wg = threadIdx.x >> 5;
+  const int c0 = (blockIdx.x * 32 + lane) * 8;
+  const int64_t r0 = ((int64_t)blockIdx.y * 4 + wg) * CONV_RPT;
+  if (c0 >= channels || r0 >= ntok) return;  // no barriers below
+  int64_t seg0, nxt;
+  if (cu != nullptr) {
+    seg0 = segment_start(cu, nseg, r0);
+    nxt = next_start(cu, nseg, r0);
+  } else {
+    seg0 = (r0 / period) * period;
+    nxt = seg0 + period;
+  }
+  uint4 raw[CONV_RPT + CONV_HALO];
+#pragma unroll
+  for (int j = 0; j < CONV_RPT + CONV_HALO; ++j) {
+    const int64_t t = r0 - CONV_HALO + j;
+    raw[j] = (t >= seg0 && t < ntok) ? ldg_stream(x + t * ldx + c0) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  float2 wr[KW][4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    if (KW == 4) {  // 2 channels x 4 taps = one aligned 16-byte load
+      float f[8];
+      unpack8(__ldg(reinterpret_cast<const uint4*>(w + (int64_t)(c0 + 2 * p) * KW)), f);
+#pragma unroll
+      for (int j = 0; j < KW; ++j) wr[j][p] = make_float2(f[j], f[KW + j]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < KW; ++j)
+        wr[j][p] = make_float2(__bfloat162float(w[(int64_t)(c0 + 2 * p) * KW + j]),
+                               __bfloat162float(w[(int64_t)(c0 + 2 * p + 1) * KW + j]));
+    }
+  }
+  bf16* dst;
+  int64_t ldd;
+  int cc;
+  if (c0 < key_dim) { dst = q; ldd = key_dim; cc = c0; }
+  else if (c0 < 2 * key_dim) { dst = k; ldd = key_dim; cc = c0 - key_dim; }
+  else { dst = v; ldd = channels - 2 * key_dim; cc = c0 - 2 * key_dim; }
+  auto as2 = [](const uint4& u, int p) {
+    const uint32_t b = p == 0 ? u.x : p == 1 ? u.y : p == 2 ? u.z : u.w;
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&b));
+  };
+  const float2 half2 = make_float2(0.5f, 0.5f);
+#pragma unroll
+  for (int i = 0; i < CONV_RPT; ++i) {
+    const int64_t t = r0 + i;
+    if (t >= ntok) break;
+    if (t == nxt) {  // a segment starts inside this row group: earlier rows are not its history
+#pragma unroll
+      for (int j = 0; j < CONV_HALO + i; ++j) raw[j] = make_uint4(0u, 0u, 0u, 0u);
+      nxt = (cu != nullptr) ? next_start(cu, nseg, t) : nxt + period;
+    }
+    uint4 out;
+    uint32_t* o = reinterpret_cast<uint32_t*>(&out);
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      float2 acc = __fmul2_rn(wr[KW - 1][p], as2(raw[CONV_HALO + i], p));
+#pragma unroll
+      for (int j = 1; j < KW; ++j) acc = __ffma2_rn(wr[KW - 1 - j][p], as2(raw[CONV_HALO + i - j], p), acc);
+      const float2 hh = __fmul2_rn(half2, acc);  // silu(x) = h + h tanh(h), h = x / 2
+      const float2 y = __ffma2_rn(hh, make_float2(tanh_approx(hh.x), tanh_approx(hh.y)), hh);
+      o[p] = pack_bf16x2(y.x, y.y);
+    }
+    *reinterpret_cast<uint4*>(dst + t * ldd + cc) = out;
+  }
+}
+
 }  // namespace fdk
 
 using namespace fdk;
@@ -185,9 +267,13 @@ extern "C" int fdk_packed_conv_silu(const void* x, int64_t ld_x, const void* wei
   const int64_t ntok = batch * seqlen;
   if (ntok == 0) return FDK_OK;
   const int64_t tiles = (ntok + CONV_ROWS - 1) / CONV_ROWS;
-  const int64_t groups = (tiles + CONV_TILES_PER_CTA - 1) / CONV_TILES_PER_CTA;
+  const int64_t cblocks = (channels + CONV_CB - 1) / CONV_CB;
+  const int64_t slots = (int64_t)sm_count() * CONV_CTAS_PER_SM;
+  const int64_t want = (tiles * cblocks + slots - 1) / slots;  // tiles per CTA for one wave
+  const int tpc = (int)(want < 1 ? 1 : want > CONV_MAX_TILES_PER_CTA ? CONV_MAX_TILES_PER_CTA : want);
+  const int64_t groups = (tiles + tpc - 1) / tpc;
   if (groups > 0x7fffffff) return set_error(FDK_ERR_UNSUPPORTED, "packed_conv: too many tokens");
-  dim3 grid((unsigned)((channels + CONV_CB - 1) / CONV_CB), (unsigned)groups);
+  dim3 grid((unsigned)cblocks, (unsigned)groups);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto xb = static_cast<const bf16*>(x);
   auto wb = static_cast<const bf16*>(weight);
@@ -206,11 +292,21 @@ extern "C" int fdk_packed_conv_silu(const void* x, int64_t ld_x, const void* wei
     cudaFuncSetAttribute(packed_conv_silu_smem_kernel<1>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (dev >= 0 && dev < 64) carveout_set[dev] = true;
   }
+  if (ntok <= CONV_DIRECT_MAX_TOKENS) {
+    const dim3 dgrid((unsigned)((channels / 8 + 31) / 32), (unsigned)((ntok + 4 * CONV_RPT - 1) / (4 * CONV_RPT)));
+    switch (kernel_width) {
+      case 4: packed_conv_silu_direct_kernel<4><<<dgrid, 128, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
+      case 3: packed_conv_silu_direct_kernel<3><<<dgrid, 128, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
+      case 2: packed_conv_silu_direct_kernel<2><<<dgrid, 128, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
+      default: packed_conv_silu_direct_kernel<1><<<dgrid, 128, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
+    }
+    return check_launch("packed_conv_silu");
+  }
   switch (kernel_width) {
-    case 4: packed_conv_silu_smem_kernel<4><<<grid, CONV_THREADS, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
-    case 3: packed_conv_silu_smem_kernel<3><<<grid, CONV_THREADS, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
-    case 2: packed_conv_silu_smem_kernel<2><<<grid, CONV_THREADS, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
-    default: packed_conv_silu_smem_kernel<1><<<grid, CONV_THREADS, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
+    case 4: packed_conv_silu_smem_kernel<4><<<grid, CONV_THREADS, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb, tpc); break;
+    case 3: packed_conv_silu_smem_kernel<3><<<grid, CONV_THREADS, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb, tpc); break;
+    case 2: packed_conv_silu_smem_kernel<2><<<grid, CONV_THREADS, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb, tpc); break;
+    default: packed_conv_silu_smem_kernel<1><<<grid, CONV_THREADS, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb, tpc); break;
   }
   return check_launch("packed_conv_silu");
 }

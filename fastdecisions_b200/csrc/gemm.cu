@@ -1,0 +1,338 @@
+// Projection / MLP GEMMs for sm_100a: C = A B^T (bf16 in, fp32 accumulate) on tcgen05 with TMEM
+// accumulators fed by TMA, with the epilogue the decision forward needs fused in.
+//
+// Persistent kernel, one CTA per SM, tiles of 128 x 256 outputs (M = 128, N = 256 MMAs) visited in
+// bands of 8 N-tiles, n fastest (consecutive tiles share an A row block).  Warp roles (192 threads):
+//   warp 0     TMA producer: A [128 rows][64 k] and B [256 rows][64 k] per k-step into a ring of
+//              STAGES stages (128-byte swizzle; 48 KB a stage)
+//   warp 1     TMEM allocator (512 columns: two 256-column accumulators) + single-thread MMA issuer
+//   warps 2-5  epilogue: thread = output row = TMEM lane; drains accumulator b while the MMAs of the
+//              next tile run into the other one, writing through shared memory with TMA stores
+// Epilogues:
+//   PLAIN   C[m][n] = bf16(acc)
+//   SWIGLU  B's rows are the gate / up projections interleaved in blocks of 128 rows (block j:
+//           gate rows [128 j, +128) then up rows [128 j, +128)), so one tile holds 128 gate and the
+//           matching 128 up columns: C[m][128 j + c] = bf16(silu(g) * u) from the fp32 accumulators
+//           ([tf]:706-708 -- the [T, 2 I] projection is never written to HBM)
+// Every mbarrier wait is bounded (see sm100.cuh); a wait that runs out sets this file's device error
+// word (bit 16 of fdk_poll_device_error's code), the CTA drains its copies and MMAs and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace fdk {
+namespace gemm {
+using namespace sm100;
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr uint32_t A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, ST_BYTES = A_BYTES + B_BYTES;
+constexpr uint32_t OUT_BOX = 32 * 128;                     // [32 rows][64 bf16] output block, 128-byte swizzle
+constexpr uint32_t OFF_OUT = STAGES * ST_BYTES;              // per epilogue warp: two OUT_BOX buffers
+constexpr uint32_t OFF_BAR = OFF_OUT + 4 * 2 * OUT_BOX;
+enum { B_FULL = 0, B_EMPTY = STAGES, B_TFULL = 2 * STAGES, B_TEMPTY = 2 * STAGES + 2, B_DRAIN = 2 * STAGES + 4,
+       NBAR = 2 * STAGES + 5 };
+constexpr uint32_t SMEM_BYTES = OFF_BAR + 8 * NBAR + 16 + 1024;
+constexpr int THREADS = 192;
+constexpr uint32_t TM_COLS = 512;
+constexpr long long DRAIN_BUDGET = 2000000000LL;
+
+enum Epi { PLAIN = 0, SWIGLU = 1 };
+
+__device__ int g_gemm_error = 0;
+
+struct Params {
+  int m, n, k;          // C is m x (n, or n / 2 for SWIGLU)
+  int m_tiles, n_tiles, k_steps;
+  int band;             // n-blocks per band of the tile order
+  bf16* c;
+  int64_t ldc;
+};
+
+// tile index -> (m block, n block): bands of p.band n-blocks, n fastest inside a band (the ~148
+// tiles in flight share a few A row blocks and the band's B blocks in L2)
+__device__ __forceinline__ void tile_coords(int t, const Params& p, int& mb, int& nb) {
+  const int band_tiles = p.band * p.m_tiles;
+  const int band = t / band_tiles, r = t - band * band_tiles;
+  const int width = min(p.band, p.n_tiles - band * p.band);
+  mb = r / width;
+  nb = band * p.band + (r - mb * width);
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(THREADS, 1)
+gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+            const __grid_constant__ CUtensorMap tc, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t bar0 = base + OFF_BAR;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + OFF_BAR + 8 * NBAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_BAR + 8 * NBAR + 4);
+  auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int num_tiles = p.m_tiles * p.n_tiles;
+
+  if (tid == 0) {
+    for (int i = 0; i < NBAR; ++i) mbar_init(bar(i), (i == B_TEMPTY || i == B_TEMPTY + 1) ? 128u : 1u);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&ta);
+      prefetch_tmap(&tb);
+      int it = 0;  // k-steps issued by this CTA (ring position)
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, p, mb, nb);
+        for (int ks = 0; ks < p.k_steps; ++ks, ++it) {
+          const int st = it % STAGES;
+          if (it >= STAGES && !mbar_wait(bar(B_EMPTY + st), ((it / STAGES) - 1) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = base + st * ST_BYTES;
+          mbar_expect_tx(bar(B_FULL + st), ST_BYTES);
+          tma_load_2d(sa, &ta, bar(B_FULL + st), ks * BK, mb * BM);
+          tma_load_2d(sa + A_BYTES, &tb, bar(B_FULL + st), ks * BK, nb * BN);
+        }
+      }
+      // every issued copy has landed before the CTA exits
+      volatile int never = 0;
+      for (int j = (it > STAGES ? it - STAGES : 0); j < it; ++j)
+        mbar_wait(bar(B_FULL + j % STAGES), (j / STAGES) & 1, &never, DRAIN_BUDGET);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IDESC = idesc_bf16(BM, BN, false, false);
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x, ++local) {
+        const int acc = local & 1;
+        // the epilogue has drained this accumulator (its previous use was tile local - 2)
+        if (local >= 2 && !mbar_wait(bar(B_TEMPTY + acc), ((local >> 1) - 1) & 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)acc * BN;
+        for (int ks = 0; ks < p.k_steps; ++ks, ++it) {
+          const int st = it % STAGES;
+          if (!mbar_wait(bar(B_FULL + st), (it / STAGES) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = base + st * ST_BYTES;
+          const uint64_t da = sdesc_sw128(sa, 16, 1024), db = sdesc_sw128(sa + A_BYTES, 16, 1024);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_ss(d, da + (uint32_t)(2 * kk), db + (uint32_t)(2 * kk), IDESC, (ks > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(bar(B_EMPTY + st));
+        }
+        if (ok) umma_commit(bar(B_TFULL + acc));
+      }
+      volatile int never = 0;
+      umma_commit(bar(B_DRAIN));
+      mbar_wait(bar(B_DRAIN), 0, &never, DRAIN_BUDGET);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2-5)
+    // Thread = output row = TMEM lane.  Each 64-column piece of the warp's 32 rows is converted to
+    // bf16 into a 128-byte-swizzled [32][64] shared-memory block and written by one TMA store
+    // (rows past m and columns past n are clipped by the tensor map); two blocks per warp alternate.
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
+    const uint32_t obuf = base + OFF_OUT + (uint32_t)q4 * 2 * OUT_BOX;
+    uint8_t* obuf_g = gbase + OFF_OUT + q4 * 2 * OUT_BOX;
+    int local = 0, pieces = 0;
+    auto put_piece = [&](const float (&f)[64], int x, int y) {
+      const int b = pieces & 1;
+      if (lane == 0 && pieces >= 2) bulk_wait_read<1>();  // the store that used buffer b is done reading
+      __syncwarp();
+      uint8_t* dst = obuf_g + b * OUT_BOX + lane * 128;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float h[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) h[i] = f[j * 8 + i];
+        *reinterpret_cast<uint4*>(dst + ((j ^ (lane & 7)) << 4)) = pack8(h);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(&tc, obuf + b * OUT_BOX, x, y);
+        bulk_commit();
+      }
+      ++pieces;
+    };
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+      const int acc = local & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(B_TFULL + acc), (local >> 1) & 1, abort_flag) ? 1 : 0)) break;
+      tc_fence_after();
+      int mb, nb;
+      tile_coords(t, p, mb, nb);
+      const int y = mb * BM + q4 * 32;
+      const uint32_t tacc = tmem + lane_addr + (uint32_t)acc * BN;
+      if constexpr (EPI == PLAIN) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          uint32_t v[2][32];
+          tmem_ld32(tacc + c * 64, v[0]);
+          tmem_ld32(tacc + c * 64 + 32, v[1]);
+          tmem_ld_wait();
+          if (c == BN / 64 - 1) {  // the accumulator is free once its last columns are in registers
+            tc_fence_before();
+            mbar_arrive(bar(B_TEMPTY + acc));
+          }
+          float f[64];
+#pragma unroll
+          for (int i = 0; i < 64; ++i) f[i] = __uint_as_float(v[i >> 5][i & 31]);
+          put_piece(f, nb * BN + c * 64, y);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 128; ++c) {
+          float f[64];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint32_t g[32], u[32];
+            tmem_ld32(tacc + c * 64 + h * 32, g);
+            tmem_ld32(tacc + BN / 2 + c * 64 + h * 32, u);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float gv = __uint_as_float(g[i]);
+              f[h * 32 + i] = gv / (1.0f + __expf(-gv)) * __uint_as_float(u[i]);
+            }
+          }
+          if (c == BN / 128 - 1) {
+            tc_fence_before();
+            mbar_arrive(bar(B_TEMPTY + acc));
+          }
+          put_piece(f, nb * (BN / 2) + c * 64, y);
+        }
+      }
+    }
+    if (lane == 0) bulk_wait<0>();  // every store has completed before the CTA exits
+    __syncwarp();
+  }
+  // ------------------------------------------------------------------ teardown
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TM_COLS);
+  }
+  if (tid == 0 && *abort_flag) atomicOr(&g_gemm_error, 1);
+}
+
+using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
+
+static EncodeFn encode_fn() {
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(ptr);
+    cudaGetLastError();
+  }
+  return fn;
+}
+
+// [rows][cols] bf16 (row stride ld elements), box 64 x box_rows, 128-byte swizzle; out-of-range
+// rows / columns read as zero (ragged m, n and k tails)
+static int kmajor_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  EncodeFn enc = encode_fn();
+  if (!enc) return set_error(FDK_ERR_DEVICE, "gemm: cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(FDK_ERR_INVALID_ARGUMENT, "gemm: tensor map encode failed (%d)", (int)r);
+  return FDK_OK;
+}
+
+}  // namespace gemm
+
+int gemm_take_device_error() {
+  int h = 0;
+  if (cudaMemcpyFromSymbol(&h, gemm::g_gemm_error, sizeof(int)) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  if (h) {
+    int zero = 0;
+    cudaMemcpyToSymbol(gemm::g_gemm_error, &zero, sizeof(int));
+  }
+  return h;
+}
+
+}  // namespace fdk
+
+using namespace fdk;
+
+extern "C" int fdk_gemm_bf16(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc, int64_t m,
+                             int64_t n, int64_t k, int epilogue, void* stream) {
+  using namespace fdk::gemm;
+  if (int st = check_device()) return st;
+  if (!a || !b || !c) return set_error(FDK_ERR_INVALID_ARGUMENT, "gemm: null pointer");
+  if (epilogue != PLAIN && epilogue != SWIGLU)
+    return set_error(FDK_ERR_INVALID_ARGUMENT, "gemm: unknown epilogue %d", epilogue);
+  if (m < 0 || n <= 0 || k <= 0 || m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff)
+    return set_error(FDK_ERR_INVALID_ARGUMENT, "gemm: bad sizes m=%lld n=%lld k=%lld", (long long)m, (long long)n,
+                     (long long)k);
+  if (n % 8 || k % 8) return set_error(FDK_ERR_ALIGNMENT, "gemm: n and k must be multiples of 8 (16-byte rows)");
+  if (epilogue == SWIGLU && n % BN)
+    return set_error(FDK_ERR_UNSUPPORTED, "gemm: the SwiGLU epilogue needs n (gate + up rows) a multiple of %d", BN);
+  const int64_t nout = epilogue == SWIGLU ? n / 2 : n;
+  if (lda < k || ldb < k || ldc < nout) return set_error(FDK_ERR_INVALID_ARGUMENT, "gemm: row stride too small");
+  if (!aligned16(a) || !aligned16(b) || !aligned16(c) || lda % 8 || ldb % 8 || ldc % 8)
+    return set_error(FDK_ERR_ALIGNMENT, "gemm: pointers and row strides must be 16-byte aligned");
+  if (m == 0) return FDK_OK;
+  CUtensorMap ma, mb, mc;
+  if (int st = kmajor_map(&ma, a, m, k, lda, BM)) return st;
+  if (int st = kmajor_map(&mb, b, n, k, ldb, BN)) return st;
+  if (int st = kmajor_map(&mc, c, m, nout, ldc, 32)) return st;  // output: [32 rows][64 cols] boxes
+  Params p;
+  p.m = (int)m;
+  p.n = (int)n;
+  p.k = (int)k;
+  p.m_tiles = (int)((m + BM - 1) / BM);
+  p.n_tiles = (int)((n + BN - 1) / BN);
+  p.k_steps = (int)((k + BK - 1) / BK);
+  p.band = 8;  // measured: sweeping every n-block first (A read from HBM once) was no faster
+  p.c = static_cast<bf16*>(c);
+  p.ldc = ldc;
+  const int64_t tiles = (int64_t)p.m_tiles * p.n_tiles;
+  if (tiles > 0x7fffffff) return set_error(FDK_ERR_UNSUPPORTED, "gemm: too many tiles");
+  const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (epilogue == SWIGLU) {
+    if (int st = ensure_smem_attr((const void*)gemm_kernel<SWIGLU>, (int)SMEM_BYTES, "gemm")) return st;
+    gemm_kernel<SWIGLU><<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, mc, p);
+  } else {
+    if (int st = ensure_smem_attr((const void*)gemm_kernel<PLAIN>, (int)SMEM_BYTES, "gemm")) return st;
+    gemm_kernel<PLAIN><<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, mc, p);
+  }
+  return check_launch("gemm");
+}

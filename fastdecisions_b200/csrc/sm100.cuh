@@ -66,6 +66,18 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* map, uint3
       "l"(map), "r"(bar), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
+// TMA tiled store from shared memory (bulk-group completion); coordinates must not be negative
+__device__ __forceinline__ void tma_store_2d(const void* map, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];\n" ::"l"(map), "r"(src),
+               "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+// waits until at most N committed bulk groups of this thread still read their shared-memory source
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read %0;\n" ::"n"(N) : "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait() { asm volatile("cp.async.bulk.wait_group %0;\n" ::"n"(N) : "memory"); }
 __device__ __forceinline__ void prefetch_tmap(const void* map) {
   asm volatile("prefetch.tensormap [%0];\n" ::"l"(map) : "memory");
 }

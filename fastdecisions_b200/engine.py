@@ -51,6 +51,7 @@ class PackedBatch:
 
 
 MAX_REQUEST_TOKENS = 32768
+FUSED_SWIGLU_MIN_TOKENS = 4096  # packed batches at least this large use the SwiGLU-fused GEMM
 
 
 def pack(requests: Sequence[Request]) -> PackedBatch:
@@ -88,13 +89,20 @@ def plan_batches(lengths: Sequence[int], max_tokens: int) -> list:
 
 class DecisionEngine:
     def __init__(self, cfg: ModelConfig, weights: dict, device="cuda", letter_ids=LETTER_IDS,
-                 temperature: float = 1.0, residual_fp32: bool = True, fuse_gdn_prologue: bool = True):
+                 temperature: float = 1.0, residual_fp32: bool = True, fuse_gdn_prologue: bool = True,
+                 fused_swiglu_gemm: bool = True):
         """``residual_fp32`` keeps the residual stream in float32 (the sum of the layer outputs is
         never rounded); with False it is stored in bf16 like the eager bf16 model.
         ``fuse_gdn_prologue`` runs the Gated-DeltaNet conv, gates and delta rule as one call on the
-        projection (same results as the three separate ops, without their HBM round trips)."""
+        projection (same results as the three separate ops, without their HBM round trips).
+        ``fused_swiglu_gemm`` runs the MLP's gate/up projection of packed batches of at least
+        ``FUSED_SWIGLU_MIN_TOKENS`` tokens as the library's tcgen05 GEMM with the SwiGLU epilogue
+        (the [T, 2 I] projection is never stored; silu(g) * u is formed from the fp32
+        accumulators): measured 1.5% more requests/s on config 5.  Smaller batches (batch-1
+        decisions) use cuBLAS and the separate SwiGLU kernel, measured faster there."""
         self.cfg = cfg
         self.fuse_gdn_prologue = bool(fuse_gdn_prologue)
+        self.fused_swiglu_gemm = bool(fused_swiglu_gemm)
         self.residual_fp32 = bool(residual_fp32)
         self.dev = torch.device(device)
         self.temperature = float(temperature)
@@ -118,6 +126,9 @@ class DecisionEngine:
             L.in_norm = put(w[p + "input_layernorm.weight"])
             L.post_norm = put(w[p + "post_attention_layernorm.weight"])
             L.w_gu = put(torch.cat([w[p + "mlp.gate_proj.weight"], w[p + "mlp.up_proj.weight"]]))
+            L.w_gu_il = None
+            if self.fused_swiglu_gemm and cfg.intermediate_size % 128 == 0:
+                L.w_gu_il = put(ops.interleave_gate_up(w[p + "mlp.gate_proj.weight"], w[p + "mlp.up_proj.weight"]))
             L.w_down = put(w[p + "mlp.down_proj.weight"])
             if kind == "linear_attention":
                 la = p + "linear_attn."
@@ -213,10 +224,14 @@ class DecisionEngine:
                 mix = torch.matmul(o.view(T, hq * D), L.w_o.t())
         with tm("residual_rmsnorm"):
             x2, _ = ops.residual_rmsnorm(mix, h, L.post_norm, c.rms_norm_eps, residual_out=h)
-        with tm("gemm"):
-            gu = torch.matmul(x2, L.w_gu.t())
-        with tm("swiglu"):
-            act = ops.swiglu(gu, c.intermediate_size)
+        if L.w_gu_il is not None and T >= FUSED_SWIGLU_MIN_TOKENS:  # gate/up GEMM + SwiGLU epilogue (own kernel)
+            with tm("gemm_swiglu"):
+                act = ops.gemm(x2, L.w_gu_il, ops.GEMM_SWIGLU)
+        else:
+            with tm("gemm"):
+                gu = torch.matmul(x2, L.w_gu.t())
+            with tm("swiglu"):
+                act = ops.swiglu(gu, c.intermediate_size)
         with tm("gemm"):
             return torch.matmul(act, L.w_down.t())
 

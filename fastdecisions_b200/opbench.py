@@ -22,7 +22,8 @@ from . import ops
 from .engine import plan_batches
 from .workloads import ModelConfig, config5_requests
 
-OPS = ("gdn_fused", "delta_rule", "gqa_attention", "packed_conv", "qk_norm_rope", "gated_rmsnorm", "residual_rmsnorm",
+CUBLAS = False  # --cublas: time torch.matmul (cuBLAS) for the gemm_* ops instead of the own GEMM
+OPS = ("gemm_gdn_in", "gemm_attn_qkv", "gemm_out", "gemm_down", "gemm_gate_up", "gemm_swiglu", "gdn_fused", "delta_rule", "gqa_attention", "packed_conv", "qk_norm_rope", "gated_rmsnorm", "residual_rmsnorm",
        "swiglu", "gdn_gates")
 
 
@@ -59,6 +60,18 @@ def make_case(op: str, lens: list, cfg: ModelConfig, seed: int = 0):
     kd, vd = Hk * Dk, Hv * Dv
     C = 2 * kd + vd
     hq, hkv, D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+    if op.startswith("gemm_"):  # own tcgen05 GEMM ("gemm_*") or, with --cublas, torch.matmul (cuBLAS)
+        H, I = cfg.hidden_size, cfg.intermediate_size
+        n, k = {"gemm_gdn_in": (C + vd + 2 * Hv, H), "gemm_attn_qkv": ((2 * hq + 2 * hkv) * D, H),
+                "gemm_out": (H, vd), "gemm_down": (H, I), "gemm_gate_up": (2 * I, H), "gemm_swiglu": (2 * I, H)}[op]
+        a, w = rn(T, k), rn(n, k, scale=0.02)
+        flops = 2.0 * T * n * k
+        if CUBLAS:
+            if op == "gemm_swiglu":  # the unfused pair: cuBLAS GEMM then the SwiGLU kernel
+                return (lambda: ops.swiglu(torch.matmul(a, w.t()), I)), ("tensor", flops)
+            return (lambda: torch.matmul(a, w.t())), ("tensor", flops)
+        epi = ops.GEMM_SWIGLU if op == "gemm_swiglu" else ops.GEMM_PLAIN
+        return (lambda: ops.gemm(a, w, epi)), ("tensor", flops)
     if op == "delta_rule":
         q, k, v = rn(1, T, Hk, Dk), rn(1, T, Hk, Dk), rn(1, T, Hv, Dv, scale=0.5)
         gg = -torch.rand(1, T, Hv, generator=g, device=dev) * 0.5
@@ -178,7 +191,10 @@ def main(argv=None):
                          "126 MB L2) instead of single calls with an L2 flush between them")
     ap.add_argument("--attn", default=None,
                     help="attention geometry hq,hkv,head_dim (e.g. 8,2,256: the reference kernel's own shape)")
+    ap.add_argument("--cublas", action="store_true", help="gemm_* ops: time torch.matmul (cuBLAS) instead")
     args = ap.parse_args(argv)
+    global CUBLAS
+    CUBLAS = args.cublas
     cfg = ModelConfig()
     if args.attn:
         hq, hkv, d = (int(x) for x in args.attn.split(","))
@@ -196,7 +212,7 @@ def main(argv=None):
         else:
             ms = time_op(fn, args.iters, args.warmup)
         achieved = work / (ms * 1e-3) / (1e12 if bound == "tensor" else 1e9)
-        print(json.dumps({"op": op, "batch": "lens" if args.lens else args.batch, "tokens": int(sum(lens)),
+        print(json.dumps({"op": op + (" (cuBLAS)" if CUBLAS and op.startswith("gemm_") else ""), "batch": "lens" if args.lens else args.batch, "tokens": int(sum(lens)),
                           "attn": [cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim],
                           "segments": len(lens),
                           "max_len": int(max(lens)), "us": round(ms * 1e3, 2), "bound": bound,

@@ -519,3 +519,41 @@ def slot_readout(hidden: torch.Tensor, slots: torch.Tensor, nopts: torch.Tensor,
                   final_norm_w.data_ptr(), int(final_norm_w.dtype == torch.float32), letters.data_ptr(), K,
                   float(eps), float(temperature), probs.data_ptr(), logits.data_ptr(), _stream(hidden))
     return probs, logits
+
+
+# ------------------------------------------------------------------------------------------------
+# Projection / MLP GEMMs on tcgen05 ([tf]:442-449, 532, 657-664, 691, 706-708)
+# ------------------------------------------------------------------------------------------------
+GEMM_PLAIN, GEMM_SWIGLU = 0, 1
+
+
+def interleave_gate_up(gate_w: torch.Tensor, up_w: torch.Tensor, block: int = 128) -> torch.Tensor:
+    """``[2 I, H]`` weight for the SwiGLU GEMM: gate / up rows interleaved in blocks of ``block``
+    (block j: gate rows ``[block j, +block)`` then the same up rows)."""
+    I, H = gate_w.shape
+    if up_w.shape != (I, H) or I % block:
+        raise ValueError(f"interleave_gate_up: gate and up must both be [I, H] with I a multiple of {block}")
+    return torch.stack([gate_w.reshape(I // block, block, H), up_w.reshape(I // block, block, H)], 1).reshape(2 * I, H)
+
+
+def gemm(a: torch.Tensor, w: torch.Tensor, epilogue: int = GEMM_PLAIN, out: Optional[torch.Tensor] = None):
+    """``a [m, k] @ w[n, k]^T`` in bf16 with fp32 accumulation (``w`` in nn.Linear layout).
+    ``epilogue=GEMM_SWIGLU``: ``w`` from ``interleave_gate_up`` and the result is
+    ``silu(a gate^T) * (a up^T)`` of shape ``[m, n / 2]``."""
+    _need_cuda(a, w, out)
+    if a.dim() != 2 or w.dim() != 2 or a.shape[1] != w.shape[1]:
+        raise ValueError("gemm: expected a [m, k] and w [n, k]")
+    if a.dtype != BF16 or w.dtype != BF16 or a.stride(1) != 1 or w.stride(1) != 1:
+        raise ValueError("gemm: a and w must be bf16 with unit column stride")
+    m, k = a.shape
+    n = w.shape[0]
+    nout = n // 2 if epilogue == GEMM_SWIGLU else n
+    if out is None:
+        out = torch.empty((m, nout), device=a.device, dtype=BF16)
+    if out.shape != (m, nout) or out.dtype != BF16 or out.stride(1) != 1:
+        raise ValueError("gemm: out must be a bf16 [m, n] (SwiGLU: [m, n / 2]) tensor with unit column stride")
+    with torch.cuda.device(a.device):
+        _lib.call("fdk_gemm_bf16", a.data_ptr(), a.stride(0) if m > 1 else k, w.data_ptr(),
+                  w.stride(0) if n > 1 else k, out.data_ptr(), out.stride(0) if m > 1 else nout, m, n, k,
+                  int(epilogue), _stream(a))
+    return out

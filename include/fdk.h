@@ -225,7 +225,7 @@ int fdk_gqa_fwd(const void* q, int64_t ld_q, const void* k, int64_t ld_k, const 
  * this word, frees its resources and returns without finishing its tile.  Bits: 1 an attention
  * wait ran out, 2 a delta-rule wait ran out, 4 the bounded-wait self-test, 8 the delta rule found
  * cu_seqlens invalid on the device (cu[0] != 0, decreasing, or cu[num_segments] != tokens) and
- * treated every segment as empty.  Synchronises with the device.
+ * treated every segment as empty, 16 a GEMM wait ran out.  Synchronises with the device.
  * No reference counterpart (the reference's Triton kernels have no device waits).
  */
 int fdk_poll_device_error(int* code);
@@ -237,6 +237,21 @@ int fdk_poll_device_error(int* code);
  * kernel returns.  The context stays usable.  No reference counterpart.
  */
 int fdk_selftest_bounded_wait(int64_t budget_cycles, void* stream);
+
+/*
+ * Projection / MLP GEMM on the tcgen05 tensor cores: C = A B^T, bf16 inputs, fp32 accumulation.
+ * Replaces the nn.Linear GEMMs of the layer ([tf]:442-449, 532, 657-664, 691, 706-708; the
+ * reference's engine runs them as cuBLAS through torch) with the epilogue fused:
+ *     A [m, k] (row stride lda), B [n, k] (row stride ldb): the weight in nn.Linear layout;
+ *     epilogue 0: C [m, n] = bf16(A B^T)                         (row stride ldc)
+ *     epilogue 1: SwiGLU, [tf]:706-708.  B holds gate_proj and up_proj rows interleaved in blocks
+ *                 of 128 (block j: gate rows 128 j .. 128 j + 127, then the same up rows), n = 2 I
+ *                 a multiple of 256; C [m, I] = bf16(silu(A gate^T) * (A up^T)) computed from the
+ *                 fp32 accumulators (the [m, 2 I] projection is never stored).
+ * n and k multiples of 8, every pointer and row stride 16-byte aligned; ragged m, n, k are handled.
+ */
+int fdk_gemm_bf16(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc,
+                  int64_t m, int64_t n, int64_t k, int epilogue, void* stream);
 
 /* Token embedding gather: out[t, :] = table[ids[t], :] ([tf]:1243).  ids int32. */
 int fdk_embed(const int32_t* ids, const void* table, int64_t vocab, int64_t hidden, void* out,

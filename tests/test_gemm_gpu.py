@@ -1,0 +1,63 @@
+"""The tcgen05 projection / MLP GEMM against a float32 PyTorch reference of the same op (and the
+SwiGLU epilogue against the oracle's swiglu of [tf]:706-708), at the layer shapes of the decision
+forward and ragged sizes."""
+import pytest
+import torch
+
+from oracle import ops as O
+
+pytestmark = pytest.mark.gpu
+
+if torch.cuda.is_available():
+    from fastdecisions_b200 import _lib, ops
+
+
+def inputs(m, n, k, seed):
+    g = torch.Generator().manual_seed(seed)
+    a = torch.randn(m, k, generator=g).bfloat16()
+    w = (0.02 * torch.randn(n, k, generator=g)).bfloat16()
+    return a, w
+
+
+def check(got, ref):
+    # bf16 output of an fp32-accumulated product: within two bf16 ulps of the fp32 reference
+    got = got.float().cpu()
+    tol = 2.0 ** -7 * ref.abs() + 1e-3 * ref.abs().max().item()
+    bad = (got - ref).abs() > tol
+    assert not bad.any(), f"{int(bad.sum())} of {bad.numel()} outside tolerance, max err {(got - ref).abs().max():.3g}"
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 256, 64), (5, 8, 8), (127, 264, 72), (300, 2048, 2048), (1536, 8224, 2048),
+                                   (1000, 5120, 2048), (777, 2048, 6144), (4097, 512, 128)])
+def test_gemm_plain(m, n, k):
+    a, w = inputs(m, n, k, m + n + k)
+    got = ops.gemm(a.cuda(), w.cuda())
+    torch.cuda.synchronize()
+    assert _lib.poll_device_error() == 0
+    check(got, a.float() @ w.float().t())
+
+
+@pytest.mark.parametrize("m,inter,k", [(1, 128, 64), (200, 256, 256), (1536, 6144, 2048), (333, 384, 136)])
+def test_gemm_swiglu_epilogue(m, inter, k):
+    a, gw = inputs(m, inter, k, 3 * m + k)
+    uw = (0.02 * torch.randn(inter, k, generator=torch.Generator().manual_seed(m))).bfloat16()
+    w = ops.interleave_gate_up(gw, uw)
+    got = ops.gemm(a.cuda(), w.cuda(), ops.GEMM_SWIGLU)
+    torch.cuda.synchronize()
+    assert _lib.poll_device_error() == 0
+    ref = O.swiglu(a.float() @ gw.float().t(), a.float() @ uw.float().t())
+    check(got, ref)
+
+
+def test_gemm_strided_rows_and_rejects():
+    a, w = inputs(100, 256, 128, 7)
+    big = torch.zeros(100, 200, dtype=torch.bfloat16)
+    big[:, 40:168] = a
+    out = torch.zeros(100, 264, dtype=torch.bfloat16, device="cuda")
+    ops.gemm(big.cuda()[:, 40:168], w.cuda(), out=out[:, :256])
+    check(out[:, :256], a.float() @ w.float().t())
+    assert (out[:, 256:] == 0).all()
+    with pytest.raises(ValueError):
+        ops.gemm(a.cuda()[:, :100], w.cuda()[:, :100].contiguous()[:, :100], ops.GEMM_SWIGLU)  # k=100 % 8 != 0
+    with pytest.raises(ValueError, match="multiple of 256"):
+        ops.gemm(a.cuda(), w.cuda()[:136].contiguous(), ops.GEMM_SWIGLU)

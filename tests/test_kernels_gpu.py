@@ -140,7 +140,9 @@ def test_packed_conv_varlen_and_strided_input():
     conv_compare(got, conv_ref(x, w, cu))
 
 
-@pytest.mark.parametrize("lens", [[1500, 900, 700], [4000, 1, 1999, 64]])  # two and four tiles a CTA
+# up to 8192 tokens the direct kernel runs; above it the shared-memory staged kernel (1-4 tiles a CTA)
+@pytest.mark.parametrize("lens", [[1500, 900, 700], [4000, 1, 1999, 64], [5000, 1, 3000, 4100, 63],
+                                  [8192, 4000, 2]])
 def test_packed_conv_tiles_per_cta(lens):
     g = gen(21)
     T = sum(lens)
@@ -149,6 +151,23 @@ def test_packed_conv_tiles_per_cta(lens):
     w = (torch.randn(6144, 4, generator=g) * 0.25).bfloat16()
     got = ops.packed_conv_qkv(dev(x), dev(w), cu_seqlens=dev(cu))
     conv_compare(got, conv_ref(x, w, cu))
+
+
+@pytest.mark.parametrize("T", [300, 9000])
+@pytest.mark.parametrize("width", [1, 2, 3])
+def test_packed_conv_narrow_kernels(T, width):
+    # causal conv widths below 4 (the C ABI takes 1-4), through both kernels
+    g = gen(40 + width)
+    x = (torch.randn(1, T, 6144, generator=g) * 0.5).bfloat16()
+    w = (torch.randn(6144, width, generator=g) * 0.4).bfloat16()
+    conv_compare(ops.packed_conv_qkv(dev(x), dev(w)), conv_ref(x, w))
+
+
+def test_packed_conv_dense_batch_above_direct_threshold():
+    g = gen(23)
+    x = (torch.randn(5, 2000, 6144, generator=g) * 0.5).bfloat16()
+    w = (torch.randn(6144, 4, generator=g) * 0.25).bfloat16()
+    conv_compare(ops.packed_conv_qkv(dev(x), dev(w)), conv_ref(x, w))
 
 
 def test_packed_conv_golden(golden):
