@@ -201,7 +201,7 @@ def delta_rule_flops(batch, cfg) -> float:
     return cfg.linear_num_value_heads * float(np.ceil(L / 64).sum()) * 11.7e6
 
 
-def op_work(cfg, batches, fused_swiglu=True) -> dict:
+def op_work(cfg, batches, fused_swiglu=True, fused_qkv=True) -> dict:
     """Algorithmic work of one step per op type: ("tensor", FLOPs) or ("hbm", bytes).  Bytes count
     each input read once and each output written once (bf16 activations, fp32 residual stream)."""
     n_att = sum(1 for t in cfg.layer_types if t == "full_attention")
@@ -213,18 +213,21 @@ def op_work(cfg, batches, fused_swiglu=True) -> dict:
     hq, hkv, D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
     T = float(sum(b.tokens for b in batches))
     S = float(sum(b.num_segments for b in batches))
-    from fastdecisions_b200.engine import FUSED_SWIGLU_MIN_TOKENS
+    from fastdecisions_b200.engine import FUSED_QKV_MIN_TOKENS, FUSED_SWIGLU_MIN_TOKENS
     T_fused = float(sum(b.tokens for b in batches if b.tokens >= FUSED_SWIGLU_MIN_TOKENS)) if fused_swiglu else 0.0
+    T_qkv = float(sum(b.tokens for b in batches if b.tokens >= FUSED_QKV_MIN_TOKENS)) if fused_qkv else 0.0
     gate_up = cfg.num_hidden_layers * 2.0 * H * 2 * I * T_fused  # MLP gate/up GEMMs run SwiGLU-fused
+    qkv = n_att * 2.0 * H * (2 * hq + 2 * hkv) * D * T_qkv       # attention projections with q/k norm fused
     w = {
-        "gemm": ("tensor", 2.0 * cfg.linear_params() * T - gate_up),   # cuBLAS projections
-        "gemm_swiglu": ("tensor", gate_up),                             # own tcgen05 GEMM + SwiGLU epilogue
+        "gemm": ("tensor", 2.0 * cfg.linear_params() * T - gate_up - qkv),  # cuBLAS projections
+        "gemm_swiglu": ("tensor", gate_up),                                  # own tcgen05 GEMM + SwiGLU epilogue
+        "gemm_qk_norm_rope": ("tensor", qkv),                                # own tcgen05 GEMM + q/k norm, RoPE
         "gqa_attention": ("tensor", n_att * sum(attention_flops(b, cfg) for b in batches)),
         "delta_rule": ("tensor", n_lin * sum(delta_rule_flops(b, cfg) for b in batches)),
         "packed_conv": ("hbm", n_lin * (T * C * 2 * 2 + C * cfg.linear_conv_kernel_dim * 2)),
         "gdn_gates": ("hbm", n_lin * T * cfg.linear_num_value_heads * (2 + 2 + 4 + 2)),
         "gated_rmsnorm": ("hbm", n_lin * T * vd * (2 + 2 + 2)),
-        "qk_norm_rope": ("hbm", n_att * T * (hq + hkv) * D * 2 * 2),
+        "qk_norm_rope": ("hbm", n_att * (T - T_qkv) * (hq + hkv) * D * 2 * 2),
         # x (bf16) + residual (fp32) read, residual (fp32) + normed (bf16) written
         "residual_rmsnorm": ("hbm", (2 * cfg.num_hidden_layers - 1) * T * H * (2 + 4 + 4 + 2) + T * H * (2 + 4 + 2)),
         "swiglu": ("hbm", cfg.num_hidden_layers * (T - T_fused) * I * (2 * 2 + 2)),  # batches not fused
@@ -422,7 +425,7 @@ def run_ours(args, world, rank, local):
     cfg = W.ModelConfig()
     threads = max(1, (os.cpu_count() or 1) // max(1, world))
     weights = W.synthetic_weights(cfg, threads=threads)
-    engine = DecisionEngine(cfg, weights, dev, fused_swiglu_gemm=not args.cublas_mlp)
+    engine = DecisionEngine(cfg, weights, dev, fused_swiglu_gemm=not args.cublas_mlp, fused_qkv_gemm=args.fused_qkv)
     timer = KernelTimer()
     engine.kernel_timer = timer
 
@@ -496,7 +499,7 @@ def run_ours(args, world, rank, local):
     timer.enabled = False
     tot = timer.totals()
     pk, pk_kind = peaks()
-    work = op_work(cfg, batches, engine.fused_swiglu_gemm)  # per step: {op: (bound, units)}
+    work = op_work(cfg, batches, engine.fused_swiglu_gemm, engine.fused_qkv_gemm)  # per step: {op: (bound, units)}
     roof = {}
     for name, (bound, units) in work.items():
         if name not in tot or tot[name]["total_ms"] <= 0:
@@ -657,6 +660,9 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=25.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--streams", type=int, default=2, help="CUDA streams the packed batches are spread over")
+    ap.add_argument("--fused-qkv", action="store_true",
+                    help="attention projection as the tcgen05 GEMM with q/k norm + RoPE fused (default: cuBLAS + "
+                         "the separate kernel, measured faster)")
     ap.add_argument("--cublas-mlp", action="store_true",
                     help="MLP gate/up projection on cuBLAS with a separate SwiGLU kernel instead of the fused GEMM")
     args = ap.parse_args()

@@ -38,13 +38,21 @@ constexpr int THREADS = 192;
 constexpr uint32_t TM_COLS = 512;
 constexpr long long DRAIN_BUDGET = 2000000000LL;
 
-enum Epi { PLAIN = 0, SWIGLU = 1 };
+enum Epi { PLAIN = 0, SWIGLU = 1, QKNORM128 = 2, QKNORM256 = 3 };
 
 __device__ int g_gemm_error = 0;
 
 struct Params {
   int m, n, k;          // C is m x (n, or n / 2 for SWIGLU)
   int m_tiles, n_tiles, k_steps;
+  // QKNORM: the attention projection [q_h gate_h]... k_0.. v_0.. (head_dim columns each)
+  int hq, hkv;
+  const bf16* q_norm_w;  // [D] offsets of the (1 + w) RMSNorm
+  const bf16* k_norm_w;
+  const int32_t* positions;
+  const float* rope;     // [max_pos][rot]: cos then sin of p * inv_freq
+  int max_pos;
+  float eps;
   int band;             // n-blocks per band of the tile order
   bf16* c;
   int64_t ldc;
@@ -63,7 +71,8 @@ __device__ __forceinline__ void tile_coords(int t, const Params& p, int& mb, int
 template <int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
-            const __grid_constant__ CUtensorMap tc, const Params p) {
+            const __grid_constant__ CUtensorMap tc, const __grid_constant__ CUtensorMap tq,
+            const __grid_constant__ CUtensorMap tk, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -159,7 +168,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
     const uint32_t obuf = base + OFF_OUT + (uint32_t)q4 * 2 * OUT_BOX;
     uint8_t* obuf_g = gbase + OFF_OUT + q4 * 2 * OUT_BOX;
     int local = 0, pieces = 0;
-    auto put_piece = [&](const float (&f)[64], int x, int y) {
+    auto put_piece = [&](const float (&f)[64], const CUtensorMap* map, int x, int y) {
       const int b = pieces & 1;
       if (lane == 0 && pieces >= 2) bulk_wait_read<1>();  // the store that used buffer b is done reading
       __syncwarp();
@@ -174,7 +183,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        tma_store_2d(&tc, obuf + b * OUT_BOX, x, y);
+        tma_store_2d(map, obuf + b * OUT_BOX, x, y);
         bulk_commit();
       }
       ++pieces;
@@ -201,9 +210,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
           float f[64];
 #pragma unroll
           for (int i = 0; i < 64; ++i) f[i] = __uint_as_float(v[i >> 5][i & 31]);
-          put_piece(f, nb * BN + c * 64, y);
+          put_piece(f, &tc, nb * BN + c * 64, y);
         }
-      } else {
+      } else if constexpr (EPI == SWIGLU) {
 #pragma unroll 1
         for (int c = 0; c < BN / 128; ++c) {
           float f[64];
@@ -223,8 +232,81 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
             tc_fence_before();
             mbar_arrive(bar(B_TEMPTY + acc));
           }
-          put_piece(f, nb * (BN / 2) + c * 64, y);
+          put_piece(f, &tc, nb * (BN / 2) + c * 64, y);
         }
+      } else {
+        // QKNORM: head blocks of D columns; q / k blocks get RMSNorm (1 + w) over the head and the
+        // rotary embedding of their first D / 4 features ([tf]:657-668), then go to q_out / k_out
+        constexpr int D = EPI == QKNORM128 ? 128 : 256, ROT = D / 4, HALF = ROT / 2;
+        const int m = mb * BM + row;
+        int pos = (m < p.m) ? p.positions[m] : 0;
+        pos = pos < 0 ? 0 : (pos >= p.max_pos ? p.max_pos - 1 : pos);
+        const float* cs = p.rope + (int64_t)pos * ROT;  // cos[0:HALF] then sin[0:HALF]
+        const int qcols = 2 * p.hq * D, kcols = p.hkv * D;
+#pragma unroll 1
+        for (int blk = 0; blk < BN / D; ++blk) {
+          const int c0 = nb * BN + blk * D;  // first column of this head block
+          if (c0 >= p.n) break;
+          const uint32_t tb0 = tacc + blk * D;
+          const bool is_q = c0 < qcols && ((c0 / D) & 1) == 0;
+          const bool is_k = c0 >= qcols && c0 < qcols + kcols;
+          if (!is_q && !is_k) {  // output gate or v: stored as computed
+#pragma unroll 1
+            for (int c = 0; c < D / 64; ++c) {
+              uint32_t v[2][32];
+              tmem_ld32(tb0 + c * 64, v[0]);
+              tmem_ld32(tb0 + c * 64 + 32, v[1]);
+              tmem_ld_wait();
+              float f[64];
+#pragma unroll
+              for (int i = 0; i < 64; ++i) f[i] = __uint_as_float(v[i >> 5][i & 31]);
+              put_piece(f, &tc, c0 + c * 64, y);
+            }
+            continue;
+          }
+          float ss = 0.f;
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld32(tb0 + c * 32, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ss = fmaf(__uint_as_float(v[i]), __uint_as_float(v[i]), ss);
+          }
+          const float inv = rsqrtf(ss / (float)D + p.eps);
+          const bf16* wn = is_q ? p.q_norm_w : p.k_norm_w;
+          const CUtensorMap* map = is_q ? &tq : &tk;
+          const int head = is_q ? c0 / (2 * D) : (c0 - qcols) / D;
+#pragma unroll 1
+          for (int c = 0; c < D / 64; ++c) {
+            uint32_t v[2][32];
+            tmem_ld32(tb0 + c * 64, v[0]);
+            tmem_ld32(tb0 + c * 64 + 32, v[1]);
+            tmem_ld_wait();
+            float f[64];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float wv[8];
+              unpack8(__ldg(reinterpret_cast<const uint4*>(wn + c * 64 + j * 8)), wv);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) f[j * 8 + i] = __uint_as_float(v[(j * 8 + i) >> 5][(j * 8 + i) & 31]) * inv * (1.0f + wv[i]);
+            }
+            if (c == 0) {  // rotate-half over the first ROT features (all inside the first piece)
+              float r[ROT];
+#pragma unroll
+              for (int i = 0; i < ROT; ++i) {
+                const int ii = i < HALF ? i : i - HALF;
+                const float cv = __ldg(cs + ii), sv = __ldg(cs + HALF + ii);
+                r[i] = i < HALF ? fmaf(f[i], cv, -f[i + HALF] * sv) : fmaf(f[i], cv, f[i - HALF] * sv);
+              }
+#pragma unroll
+              for (int i = 0; i < ROT; ++i) f[i] = r[i];
+            }
+            put_piece(f, map, head * D + c * 64, y);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(bar(B_TEMPTY + acc));
       }
     }
     if (lane == 0) bulk_wait<0>();  // every store has completed before the CTA exits
@@ -313,7 +395,7 @@ extern "C" int fdk_gemm_bf16(const void* a, int64_t lda, const void* b, int64_t 
   if (int st = kmajor_map(&ma, a, m, k, lda, BM)) return st;
   if (int st = kmajor_map(&mb, b, n, k, ldb, BN)) return st;
   if (int st = kmajor_map(&mc, c, m, nout, ldc, 32)) return st;  // output: [32 rows][64 cols] boxes
-  Params p;
+  Params p{};
   p.m = (int)m;
   p.n = (int)n;
   p.k = (int)k;
@@ -329,10 +411,73 @@ extern "C" int fdk_gemm_bf16(const void* a, int64_t lda, const void* b, int64_t 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (epilogue == SWIGLU) {
     if (int st = ensure_smem_attr((const void*)gemm_kernel<SWIGLU>, (int)SMEM_BYTES, "gemm")) return st;
-    gemm_kernel<SWIGLU><<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, mc, p);
+    gemm_kernel<SWIGLU><<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, mc, mc, mc, p);
   } else {
     if (int st = ensure_smem_attr((const void*)gemm_kernel<PLAIN>, (int)SMEM_BYTES, "gemm")) return st;
-    gemm_kernel<PLAIN><<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, mc, p);
+    gemm_kernel<PLAIN><<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, mc, mc, mc, p);
   }
   return check_launch("gemm");
+}
+
+extern "C" int fdk_gemm_bf16_qk_norm_rope(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc,
+                                          int64_t m, int64_t n, int64_t k, int64_t hq, int64_t hkv, int64_t head_dim,
+                                          const void* q_norm_w, const void* k_norm_w, const int32_t* positions,
+                                          const float* rope_table, int64_t max_pos, int rot_dim, float eps, void* q_out,
+                                          void* k_out, void* stream) {
+  using namespace fdk::gemm;
+  if (int st = check_device()) return st;
+  if (!a || !b || !c || !q_norm_w || !k_norm_w || !positions || !rope_table || !q_out || !k_out)
+    return set_error(FDK_ERR_INVALID_ARGUMENT, "gemm_qk_norm_rope: null pointer");
+  if (head_dim != 128 && head_dim != 256)
+    return set_error(FDK_ERR_UNSUPPORTED, "gemm_qk_norm_rope: head_dim=%lld (128 or 256)", (long long)head_dim);
+  if (rot_dim != head_dim / 4)
+    return set_error(FDK_ERR_UNSUPPORTED, "gemm_qk_norm_rope: rot_dim must be head_dim / 4 (partial rotary factor 0.25)");
+  if (hq < 1 || hkv < 1 || hq > 4096 || hkv > 4096 || max_pos < 1 || max_pos > 0x7fffffff)
+    return set_error(FDK_ERR_INVALID_ARGUMENT, "gemm_qk_norm_rope: bad head counts or max_pos");
+  if (n != (2 * hq + 2 * hkv) * head_dim)
+    return set_error(FDK_ERR_INVALID_ARGUMENT, "gemm_qk_norm_rope: n must be (2 hq + 2 hkv) x head_dim");
+  if (m < 0 || k <= 0 || m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff)
+    return set_error(FDK_ERR_INVALID_ARGUMENT, "gemm_qk_norm_rope: bad sizes");
+  if (k % 8) return set_error(FDK_ERR_ALIGNMENT, "gemm_qk_norm_rope: k must be a multiple of 8");
+  if (lda < k || ldb < k || ldc < n) return set_error(FDK_ERR_INVALID_ARGUMENT, "gemm_qk_norm_rope: row stride too small");
+  if (!aligned16(a) || !aligned16(b) || !aligned16(c) || !aligned16(q_out) || !aligned16(k_out) || !aligned16(q_norm_w) ||
+      !aligned16(k_norm_w) || lda % 8 || ldb % 8 || ldc % 8)
+    return set_error(FDK_ERR_ALIGNMENT, "gemm_qk_norm_rope: pointers and row strides must be 16-byte aligned");
+  if (m == 0) return FDK_OK;
+  CUtensorMap ma, mb, mc, mq, mk;
+  if (int st = kmajor_map(&ma, a, m, k, lda, BM)) return st;
+  if (int st = kmajor_map(&mb, b, n, k, ldb, BN)) return st;
+  if (int st = kmajor_map(&mc, c, m, n, ldc, 32)) return st;
+  if (int st = kmajor_map(&mq, q_out, m, hq * head_dim, hq * head_dim, 32)) return st;
+  if (int st = kmajor_map(&mk, k_out, m, hkv * head_dim, hkv * head_dim, 32)) return st;
+  Params p{};
+  p.m = (int)m;
+  p.n = (int)n;
+  p.k = (int)k;
+  p.m_tiles = (int)((m + BM - 1) / BM);
+  p.n_tiles = (int)((n + BN - 1) / BN);
+  p.k_steps = (int)((k + BK - 1) / BK);
+  p.band = 8;
+  p.c = static_cast<bf16*>(c);
+  p.ldc = ldc;
+  p.hq = (int)hq;
+  p.hkv = (int)hkv;
+  p.q_norm_w = static_cast<const bf16*>(q_norm_w);
+  p.k_norm_w = static_cast<const bf16*>(k_norm_w);
+  p.positions = positions;
+  p.rope = rope_table;
+  p.max_pos = (int)max_pos;
+  p.eps = eps;
+  const int64_t tiles = (int64_t)p.m_tiles * p.n_tiles;
+  if (tiles > 0x7fffffff) return set_error(FDK_ERR_UNSUPPORTED, "gemm_qk_norm_rope: too many tiles");
+  const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (head_dim == 128) {
+    if (int st = ensure_smem_attr((const void*)gemm_kernel<QKNORM128>, (int)SMEM_BYTES, "gemm_qk_norm_rope")) return st;
+    gemm_kernel<QKNORM128><<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, mc, mq, mk, p);
+  } else {
+    if (int st = ensure_smem_attr((const void*)gemm_kernel<QKNORM256>, (int)SMEM_BYTES, "gemm_qk_norm_rope")) return st;
+    gemm_kernel<QKNORM256><<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, mc, mq, mk, p);
+  }
+  return check_launch("gemm_qk_norm_rope");
 }

@@ -52,6 +52,7 @@ class PackedBatch:
 
 MAX_REQUEST_TOKENS = 32768
 FUSED_SWIGLU_MIN_TOKENS = 4096  # packed batches at least this large use the SwiGLU-fused GEMM
+FUSED_QKV_MIN_TOKENS = 4096     # ... and the attention projection with q/k norm + RoPE fused
 
 
 def pack(requests: Sequence[Request]) -> PackedBatch:
@@ -90,7 +91,7 @@ def plan_batches(lengths: Sequence[int], max_tokens: int) -> list:
 class DecisionEngine:
     def __init__(self, cfg: ModelConfig, weights: dict, device="cuda", letter_ids=LETTER_IDS,
                  temperature: float = 1.0, residual_fp32: bool = True, fuse_gdn_prologue: bool = True,
-                 fused_swiglu_gemm: bool = True):
+                 fused_swiglu_gemm: bool = True, fused_qkv_gemm: bool = False):
         """``residual_fp32`` keeps the residual stream in float32 (the sum of the layer outputs is
         never rounded); with False it is stored in bf16 like the eager bf16 model.
         ``fuse_gdn_prologue`` runs the Gated-DeltaNet conv, gates and delta rule as one call on the
@@ -99,10 +100,16 @@ class DecisionEngine:
         ``FUSED_SWIGLU_MIN_TOKENS`` tokens as the library's tcgen05 GEMM with the SwiGLU epilogue
         (the [T, 2 I] projection is never stored; silu(g) * u is formed from the fp32
         accumulators): measured 1.5% more requests/s on config 5.  Smaller batches (batch-1
-        decisions) use cuBLAS and the separate SwiGLU kernel, measured faster there."""
+        decisions) use cuBLAS and the separate SwiGLU kernel, measured faster there.
+        ``fused_qkv_gemm`` likewise runs the attention projection of batches of at least
+        ``FUSED_QKV_MIN_TOKENS`` tokens as the tcgen05 GEMM whose epilogue applies the q / k RMSNorm
+        and the partial RoPE (no separate q / k norm kernel, no bf16 rounding of q / k before it).
+        Off by default: measured 10% slower than cuBLAS + the separate kernel at 32k tokens (the
+        GEMM's mainloop is ~7% behind cuBLAS at N = 5120)."""
         self.cfg = cfg
         self.fuse_gdn_prologue = bool(fuse_gdn_prologue)
         self.fused_swiglu_gemm = bool(fused_swiglu_gemm)
+        self.fused_qkv_gemm = bool(fused_qkv_gemm)
         self.residual_fp32 = bool(residual_fp32)
         self.dev = torch.device(device)
         self.temperature = float(temperature)
@@ -213,10 +220,16 @@ class DecisionEngine:
             with tm("gemm"):
                 mix = torch.matmul(on, L.w_out.t())
         else:
-            with tm("gemm"):
-                proj = torch.matmul(x, L.w_qkv.t())                                      # [T, (2 hq + 2 hkv) D]
-            with tm("qk_norm_rope"):
-                q, k = ops.attn_qk_norm_rope(proj, L.q_norm, L.k_norm, pos, self.rope, hq, hkv, D, c.rms_norm_eps)
+            if (self.fused_qkv_gemm and T >= FUSED_QKV_MIN_TOKENS and D in (128, 256)
+                    and self.rope.shape[1] == D // 4):
+                with tm("gemm_qk_norm_rope"):  # projection + q/k norm + RoPE (own tcgen05 GEMM)
+                    proj, q, k = ops.gemm_qk_norm_rope(x, L.w_qkv, L.q_norm, L.k_norm, pos, self.rope, hq, hkv, D,
+                                                       c.rms_norm_eps)
+            else:
+                with tm("gemm"):
+                    proj = torch.matmul(x, L.w_qkv.t())                                  # [T, (2 hq + 2 hkv) D]
+                with tm("qk_norm_rope"):
+                    q, k = ops.attn_qk_norm_rope(proj, L.q_norm, L.k_norm, pos, self.rope, hq, hkv, D, c.rms_norm_eps)
             v = proj[:, (2 * hq + hkv) * D:].view(T, hkv, D)
             with tm("gqa_attention"):
                 o = ops.gqa_attention_varlen_(q, k, v, cu, max_seqlen, gate=proj[:, D:], gate_interleaved=True)

@@ -23,7 +23,7 @@ from .engine import plan_batches
 from .workloads import ModelConfig, config5_requests
 
 CUBLAS = False  # --cublas: time torch.matmul (cuBLAS) for the gemm_* ops instead of the own GEMM
-OPS = ("gemm_gdn_in", "gemm_attn_qkv", "gemm_out", "gemm_down", "gemm_gate_up", "gemm_swiglu", "gdn_fused", "delta_rule", "gqa_attention", "packed_conv", "qk_norm_rope", "gated_rmsnorm", "residual_rmsnorm",
+OPS = ("gemm_qkv_norm_rope", "gemm_gdn_in", "gemm_attn_qkv", "gemm_out", "gemm_down", "gemm_gate_up", "gemm_swiglu", "gdn_fused", "delta_rule", "gqa_attention", "packed_conv", "qk_norm_rope", "gated_rmsnorm", "residual_rmsnorm",
        "swiglu", "gdn_gates")
 
 
@@ -63,6 +63,7 @@ def make_case(op: str, lens: list, cfg: ModelConfig, seed: int = 0):
     if op.startswith("gemm_"):  # own tcgen05 GEMM ("gemm_*") or, with --cublas, torch.matmul (cuBLAS)
         H, I = cfg.hidden_size, cfg.intermediate_size
         n, k = {"gemm_gdn_in": (C + vd + 2 * Hv, H), "gemm_attn_qkv": ((2 * hq + 2 * hkv) * D, H),
+                "gemm_qkv_norm_rope": ((2 * hq + 2 * hkv) * D, H),
                 "gemm_out": (H, vd), "gemm_down": (H, I), "gemm_gate_up": (2 * I, H), "gemm_swiglu": (2 * I, H)}[op]
         a, w = rn(T, k), rn(n, k, scale=0.02)
         flops = 2.0 * T * n * k
@@ -70,6 +71,13 @@ def make_case(op: str, lens: list, cfg: ModelConfig, seed: int = 0):
             if op == "gemm_swiglu":  # the unfused pair: cuBLAS GEMM then the SwiGLU kernel
                 return (lambda: ops.swiglu(torch.matmul(a, w.t()), I)), ("tensor", flops)
             return (lambda: torch.matmul(a, w.t())), ("tensor", flops)
+        if op == "gemm_qkv_norm_rope":  # the attention projection with q/k norm + RoPE
+            qn, kn = rn(D, scale=0.02), rn(D, scale=0.02)
+            rope = ops.rope_table(ops.rope_inv_freq(D, cfg.partial_rotary_factor, cfg.rope_theta).to(dev), int(L.max()))
+            if CUBLAS:
+                return (lambda: ops.attn_qk_norm_rope(torch.matmul(a, w.t()), qn, kn, pos, rope, hq, hkv, D,
+                                                      cfg.rms_norm_eps)), ("tensor", flops)
+            return (lambda: ops.gemm_qk_norm_rope(a, w, qn, kn, pos, rope, hq, hkv, D, cfg.rms_norm_eps)), ("tensor", flops)
         epi = ops.GEMM_SWIGLU if op == "gemm_swiglu" else ops.GEMM_PLAIN
         return (lambda: ops.gemm(a, w, epi)), ("tensor", flops)
     if op == "delta_rule":

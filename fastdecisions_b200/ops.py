@@ -557,3 +557,29 @@ def gemm(a: torch.Tensor, w: torch.Tensor, epilogue: int = GEMM_PLAIN, out: Opti
                   w.stride(0) if n > 1 else k, out.data_ptr(), out.stride(0) if m > 1 else nout, m, n, k,
                   int(epilogue), _stream(a))
     return out
+
+
+def gemm_qk_norm_rope(a: torch.Tensor, w: torch.Tensor, q_norm_w: torch.Tensor, k_norm_w: torch.Tensor,
+                      positions: torch.Tensor, rope: torch.Tensor, hq: int, hkv: int, head_dim: int,
+                      eps: float = 1e-6):
+    """Attention projection ``a [m, k] @ w[(2 hq + 2 hkv) D, k]^T`` with q/k RMSNorm (1 + w) and partial
+    RoPE fused: returns ``(proj [m, n], q [m, hq, D], k [m, hkv, D])``; ``proj`` holds the output
+    gate and v columns (its q / k columns are not written)."""
+    _need_cuda(a, w, q_norm_w, k_norm_w, positions, rope)
+    m, k = a.shape
+    n = w.shape[0]
+    if a.dtype != BF16 or w.dtype != BF16 or a.stride(1) != 1 or w.stride(1) != 1 or w.shape[1] != k:
+        raise ValueError("gemm_qk_norm_rope: a [m, k] and w [n, k] must be bf16 with unit column stride")
+    if q_norm_w.dtype != BF16 or k_norm_w.dtype != BF16 or positions.dtype != torch.int32:
+        raise ValueError("gemm_qk_norm_rope: bf16 norm weights and int32 positions expected")
+    if rope.dim() != 2 or rope.dtype != torch.float32 or not rope.is_contiguous():
+        raise ValueError("gemm_qk_norm_rope: rope must be a contiguous float32 [max_pos, rot_dim] table")
+    proj = torch.empty((m, n), device=a.device, dtype=BF16)
+    q = torch.empty((m, hq, head_dim), device=a.device, dtype=BF16)
+    kk = torch.empty((m, hkv, head_dim), device=a.device, dtype=BF16)
+    with torch.cuda.device(a.device):
+        _lib.call("fdk_gemm_bf16_qk_norm_rope", a.data_ptr(), a.stride(0) if m > 1 else k, w.data_ptr(),
+                  w.stride(0) if n > 1 else k, proj.data_ptr(), n, m, n, k, hq, hkv, head_dim, q_norm_w.data_ptr(),
+                  k_norm_w.data_ptr(), positions.data_ptr(), rope.data_ptr(), rope.shape[0], rope.shape[1], float(eps),
+                  q.data_ptr(), kk.data_ptr(), _stream(a))
+    return proj, q, kk

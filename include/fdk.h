@@ -253,6 +253,25 @@ int fdk_selftest_bounded_wait(int64_t budget_cycles, void* stream);
 int fdk_gemm_bf16(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc,
                   int64_t m, int64_t n, int64_t k, int epilogue, void* stream);
 
+/*
+ * The attention layer's projection GEMM with its prologue ops fused into the epilogue: C = A B^T
+ * as fdk_gemm_bf16 (B = [q_proj; k_proj; v_proj] weights, q_proj rows laid out per head as the
+ * query then the output gate, [tf]:657-659), and for every query and key head block of the result:
+ * RMSNorm with (1 + w) over the head ([tf]:662-663) and the rotary embedding of its first
+ * rot_dim = head_dim / 4 features ([tf]:666-667), computed from the fp32 accumulators, written to
+ * q_out [m, hq, head_dim] and k_out [m, hkv, head_dim] (contiguous).  C [m, n] (row stride ldc)
+ * receives the output-gate and v columns; its q and k columns are not written.  Replaces the
+ * GEMM + fdk_attn_qk_norm_rope pair (same arithmetic, without rounding q / k to bf16 before the
+ * norm).  n = (2 hq + 2 hkv) head_dim; head_dim 128 or 256; positions, rope_table and max_pos as
+ * fdk_attn_qk_norm_rope; norm weights bf16 [head_dim].
+ */
+int fdk_gemm_bf16_qk_norm_rope(const void* a, int64_t lda, const void* b, int64_t ldb, void* c,
+                               int64_t ldc, int64_t m, int64_t n, int64_t k, int64_t hq,
+                               int64_t hkv, int64_t head_dim, const void* q_norm_w,
+                               const void* k_norm_w, const int32_t* positions,
+                               const float* rope_table, int64_t max_pos, int rot_dim, float eps,
+                               void* q_out, void* k_out, void* stream);
+
 /* Token embedding gather: out[t, :] = table[ids[t], :] ([tf]:1243).  ids int32. */
 int fdk_embed(const int32_t* ids, const void* table, int64_t vocab, int64_t hidden, void* out,
               int64_t tokens, void* stream);

@@ -61,3 +61,32 @@ def test_gemm_strided_rows_and_rejects():
         ops.gemm(a.cuda()[:, :100], w.cuda()[:, :100].contiguous()[:, :100], ops.GEMM_SWIGLU)  # k=100 % 8 != 0
     with pytest.raises(ValueError, match="multiple of 256"):
         ops.gemm(a.cuda(), w.cuda()[:136].contiguous(), ops.GEMM_SWIGLU)
+
+
+@pytest.mark.parametrize("m,hq,hkv,D", [(45, 16, 4, 128), (300, 16, 4, 128), (1537, 16, 4, 128), (200, 8, 2, 256),
+                                        (130, 6, 2, 128)])
+def test_gemm_qk_norm_rope_epilogue(m, hq, hkv, D):
+    """The attention projection with q / k RMSNorm (1 + w) and partial RoPE in the epilogue, against
+    the oracle applied to the float32 product ([tf]:657-668)."""
+    g = torch.Generator().manual_seed(m + D)
+    k = 512
+    n = (2 * hq + 2 * hkv) * D
+    a = torch.randn(m, k, generator=g).bfloat16()
+    w = (0.05 * torch.randn(n, k, generator=g)).bfloat16()
+    qw = (0.1 * torch.randn(D, generator=g)).bfloat16()
+    kw = (0.1 * torch.randn(D, generator=g)).bfloat16()
+    pos = torch.cat([torch.arange(m // 2), torch.arange(m - m // 2)]).int()
+    rope = ops.rope_table(ops.rope_inv_freq(D).cuda(), max(m, 64))
+    proj, q, kk = ops.gemm_qk_norm_rope(a.cuda(), w.cuda(), qw.cuda(), kw.cuda(), pos.cuda(), rope, hq, hkv, D)
+    torch.cuda.synchronize()
+    assert _lib.poll_device_error() == 0
+    full = a.float() @ w.float().t()
+    qg = full[:, :2 * hq * D].reshape(m, hq, 2, D)
+    cos, sin = O.rope_cos_sin(pos, D)
+    q_ref = O.apply_partial_rope(O.rmsnorm_offset(qg[:, :, 0], qw), cos, sin)
+    k_ref = O.apply_partial_rope(O.rmsnorm_offset(full[:, 2 * hq * D:(2 * hq + hkv) * D].reshape(m, hkv, D), kw), cos, sin)
+    torch.testing.assert_close(q.cpu().float(), q_ref, rtol=0.008, atol=0.004)
+    torch.testing.assert_close(kk.cpu().float(), k_ref, rtol=0.008, atol=0.004)
+    # the output gate and v columns are the plain product
+    check(proj.reshape(m, -1)[:, :2 * hq * D].reshape(m, hq, 2, D)[:, :, 1], qg[:, :, 1])
+    check(proj[:, (2 * hq + hkv) * D:], full[:, (2 * hq + hkv) * D:])
