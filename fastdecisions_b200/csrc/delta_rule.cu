@@ -40,27 +40,29 @@ constexpr size_t CH_BYTES = 4 * TILE128 + TILE64 + 16;
 __host__ __device__ inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 struct WsLayout {
-  size_t off_table, off_info, off_tiles, total;
+  size_t off_table, off_info, off_tiles, off_ready, total;
   int64_t max_chunks;
 };
 
-// chunk table [nseg + 1] + work counter, chunk info (first token, length, segment start)
-// [max_chunks], tiles
+// chunk table [nseg + 1] + recurrence work counter + prep tile counter, chunk info (first token,
+// length, segment start) [max_chunks], tiles [max_chunks][heads], tile-ready flags [max_chunks][heads]
 __host__ __device__ inline WsLayout ws_layout(int64_t tokens, int64_t nseg, int64_t heads) {
   WsLayout l;
   l.max_chunks = (tokens + DR_C - 1) / DR_C + nseg;
   l.off_table = 0;
-  l.off_info = align256((size_t)(nseg + 2) * 4);
+  l.off_info = align256((size_t)(nseg + 3) * 4);
   l.off_tiles = l.off_info + align256((size_t)l.max_chunks * 16);
-  l.total = l.off_tiles + align256((size_t)l.max_chunks * heads * CH_BYTES);
+  l.off_ready = l.off_tiles + align256((size_t)l.max_chunks * heads * CH_BYTES);
+  l.total = l.off_ready + align256((size_t)l.max_chunks * heads * 4);
   return l;
 }
 
 __device__ int g_delta_error = 0;  // bit 0: a bounded wait ran out; bit 1: cu_seqlens rejected on the device
 
 // One CTA of 256 threads: exclusive scan of ceil(len / 64) over segments (table[s] = first chunk
-// of segment s, table[nseg] = chunk count), each chunk's (first token, length, segment start), and the zeroed
-// work counter of the recurrence (table[nseg + 1]).
+// of segment s, table[nseg] = chunk count), each chunk's (first token, length, segment start), the zeroed
+// work counters of the recurrence (table[nseg + 1]) and of the pipelined prep (table[nseg + 2]), and
+// the zeroed tile-ready flags (`ready`, n_ready of them).
 // cu_seqlens lives on the device, so the host cannot check it: this kernel does.  Unless
 // cu[0] == 0, cu is non-decreasing and cu[nseg] == tokens (which bounds the chunk count by
 // max_chunks, the size the workspace was laid out for), it writes an all-zero table -- every
@@ -68,14 +70,16 @@ __device__ int g_delta_error = 0;  // bit 0: a bounded wait ran out; bit 1: cu_s
 // of the delta-rule error word.
 __global__ void __launch_bounds__(256) chunk_table_kernel(const int32_t* __restrict__ cu, int nseg, int64_t tokens,
                                                           int64_t max_chunks, int32_t* __restrict__ table,
-                                                          int4* __restrict__ info) {
+                                                          int4* __restrict__ info, int32_t* __restrict__ ready,
+                                                          int64_t n_ready) {
   __shared__ int warp_sums[8];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int64_t i = tid; i < n_ready; i += 256) ready[i] = 0;
   bool bad = false;
   for (int s = tid; s < nseg; s += 256) bad |= cu[s + 1] < cu[s];
   if (tid == 0) bad |= cu[0] != 0 || (int64_t)cu[nseg] != tokens;
   if (__syncthreads_or(bad)) {
-    for (int s = tid; s <= nseg + 1; s += 256) table[s] = 0;
+    for (int s = tid; s <= nseg + 2; s += 256) table[s] = 0;
     if (tid == 0) atomicOr(&g_delta_error, 2);
     return;
   }
@@ -114,6 +118,7 @@ __global__ void __launch_bounds__(256) chunk_table_kernel(const int32_t* __restr
   if (tid == 0) {
     table[nseg] = carry;
     table[nseg + 1] = 0;  // work counter of the recurrence
+    table[nseg + 2] = 0;  // tile counter of the pipelined prep
   }
 }
 
@@ -300,17 +305,34 @@ __device__ __forceinline__ void conv_rows(const uint8_t* box, int row0, int chun
 }
 constexpr uint32_t RAW_BOX = 67 * 128;  // one raw projection box: 67 rows x 64 bf16
 
-template <bool CONV>
-__global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
-    const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
-    const __grid_constant__ CUtensorMap mv, const PrepIn in, const int4* __restrict__ info,
-    const int32_t* __restrict__ table, int nseg, int heads, float scale, uint8_t* __restrict__ tiles) {
-  extern __shared__ uint8_t smem_raw[];
-  const int ci = blockIdx.x, h = blockIdx.y;
-  if (ci >= table[nseg]) return;  // CTA-uniform, before any barrier or TMEM use
-  const uint32_t raw = smem_u32(smem_raw);
-  const uint32_t base = (raw + 1023u) & ~1023u;
-  uint8_t* sb = smem_raw + (base - raw);
+// Block-wide barrier of the prep: the whole CTA (standalone kernel), or named barrier 1 over the
+// 256 prep threads of a pipelined CTA (its other warps never take part in a prep tile).
+template <bool PIPE>
+__device__ __forceinline__ void prep_sync() {
+  if constexpr (PIPE) asm volatile("bar.sync 1, 256;\n" ::: "memory");
+  else __syncthreads();
+}
+template <bool PIPE>
+__device__ __forceinline__ bool prep_sync_and(bool v) {
+  if constexpr (PIPE) {
+    uint32_t r;
+    asm volatile("{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, 256, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+                 : "=r"(r) : "r"((uint32_t)v) : "memory");
+    return r != 0;
+  } else {
+    return __syncthreads_and(v) != 0;
+  }
+}
+
+// One (chunk ci, head h) tile of the prep by 256 threads (tid 0-255).  Shared memory at `base`
+// (1024-byte aligned; `sb` its generic address) with this file's prep layout and its barriers
+// initialised; `tmem` holds TM_COLS allocated columns; `par` is the phase parity of this tile on
+// every barrier (each completes once per tile).  Returns false if a bounded wait ran out.
+template <bool CONV, bool PIPE>
+__device__ __forceinline__ bool prep_tile(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                                          const PrepIn& in, const int4* __restrict__ info, int heads, float scale,
+                                          uint8_t* __restrict__ tiles, int ci, int h, uint32_t base, uint8_t* sb,
+                                          uint32_t tmem, uint32_t par) {
   float* G2 = reinterpret_cast<float*>(sb + VEC);  // G * log2(e)
   float* bet = G2 + 64;                            // beta (0 past the chunk's length)
   float* fw = G2 + 128;                            // beta e^G
@@ -319,25 +341,10 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
   float* Tf = reinterpret_cast<float*>(sb + TF);
   const uint32_t bar0 = base + BARS;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sb + BARS + 8 * NBAR);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sb + BARS + 8 * NBAR + 4);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int4 inf = info[ci];
   const int t0 = inf.x, len = inf.y, seg_start = inf.z;
   uint8_t* tile = tiles + ((size_t)ci * heads + h) * CH_BYTES;
-
-  if (tid == 0) {
-    for (int i = 0; i < NBAR; ++i) mbar_init(bar0 + 8 * i, 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (warp == 0) {
-    tmem_alloc(smem_u32(tmem_slot), TM_COLS);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
   bool issued_v = false, issued_mma = false;
 
   // 1. raw k rows -> A1 rows 0-63, raw q rows -> rows 64-127 (TMA, 128-byte swizzle; rows past
@@ -402,7 +409,7 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
     fw[r1] = b1 * expf(G1);
     if (lane == 31) *reinterpret_cast<float*>(tile + OFF_GAMMA) = expf(G1);
   }
-  bool ok = mbar_wait(bar0 + 8 * B_QK, 0, abort_flag);
+  bool ok = mbar_wait(bar0 + 8 * B_QK, par, abort_flag);
   if (CONV && ok) {  // q (A1 rows 64-127) and k (rows 0-63): thread = 8 channels x 8 tokens
     const int g8 = tid & 31, rs = tid >> 5;
     const bool isk = g8 >= 16;
@@ -413,7 +420,7 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
     conv_rows<8>(box, rs * 8, c16 & 7, first_valid, wcol, sb + A1, (isk ? 0 : 64) + rs * 8, c16);
     fence_proxy_async_smem();  // the raw boxes are refilled by TMA (V) below
   }
-  ok = __syncthreads_and(ok) != 0;  // also publishes G2 / beta / fw
+  ok = prep_sync_and<PIPE>(ok);  // also publishes G2 / beta / fw
   if (CONV && ok && tid == 0) {  // raw v columns -> the T area, landing while k / q are normalised
     mbar_expect_tx(bar0 + 8 * B_V, 2 * RAW_BOX);
     tma_load_2d(base + TF, &mq, bar0 + 8 * B_V, 2 * in.key_dim + h * DR_D, t0 - 3);
@@ -470,7 +477,7 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
     }
     fence_proxy_async_smem();
   }
-  __syncthreads();
+  prep_sync<PIPE>();
 
   // 3. D1 = [K^; Q^] K^T  (M128 N64 K128; B is A's first 64 rows)
   if (ok && tid == 0) {
@@ -484,10 +491,10 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
     umma_commit(bar0 + 8 * B_MMA1);
     issued_mma = true;
   }
-  if (ok) ok = warp_wait(bar0 + 8 * B_MMA1, 0, abort_flag);
+  if (ok) ok = warp_wait(bar0 + 8 * B_MMA1, par, abort_flag);
   if (ok) tc_fence_after();
   // V rows -> A1 rows 64-127 (q^ is no longer read), landing while the solve runs
-  if (CONV && ok) ok = warp_wait(bar0 + 8 * B_V, 0, abort_flag);
+  if (CONV && ok) ok = warp_wait(bar0 + 8 * B_V, par, abort_flag);
   if (CONV && ok) {  // v by conv into A1 rows 64-127: thread = 8 channels x 4 tokens
     const int g8 = tid & 15, rs = tid >> 4;
     const int first_valid = max(0, seg_start - (t0 - 3));
@@ -562,7 +569,7 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
     }
   }
   tc_fence_before();
-  __syncthreads();
+  prep_sync<PIPE>();
 
   // 5. T = (I - L)^-1 in fp32.
   //    Level 0 (warps 0-1, thread = one column k of one diagonal block b): forward substitution
@@ -597,7 +604,7 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
 #pragma unroll
     for (int r = 0; r < 16; ++r) tcol[r * LDF] = x[r];
   }
-  __syncthreads();
+  prep_sync<PIPE>();
   auto blk = [&](float* base_, int bi, int bj) { return base_ + (16 * bi) * LDF + 16 * bj; };
   // level 1: warp 0 -> T_10, warp 1 -> T_32
   if (ok && warp < 2) {
@@ -612,7 +619,7 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
     bmm16_acc(acc, blk(Tf, i, i), M, LDF);
     bmm16_store(acc, blk(Tf, i, j), LDF);
   }
-  __syncthreads();
+  prep_sync<PIPE>();
   // level 2: X_ij (i in {2,3}, j in {0,1}) = L_i0 T_0j + L_i1 T_1j (T_01 = 0) into L's block (j, i)
   if (ok && warp < 4) {
     const int i = 2 + (warp >> 1), j = warp & 1;
@@ -622,7 +629,7 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
     bmm16_acc(acc, blk(Lf, i, 1), blk(Tf, 1, j), LDF);
     bmm16_store(acc, blk(Lf, j, i), LDF);
   }
-  __syncthreads();
+  prep_sync<PIPE>();
   // level 3: T_ij = T_i2 X_2j + T_i3 X_3j (T_23 = 0)
   if (ok && warp < 4) {
     const int i = 2 + (warp >> 1), j = warp & 1;
@@ -632,7 +639,7 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
     if (i == 3) bmm16_acc(acc, blk(Tf, 3, 3), blk(Lf, j, 3), LDF);
     bmm16_store(acc, blk(Tf, i, j), LDF);
   }
-  __syncthreads();
+  prep_sync<PIPE>();
 
   // 6. TU = bf16(T diag(beta)), TW = bf16(T diag(beta e^G)) as K-major swizzled B tiles (over L)
   if (ok) {
@@ -655,11 +662,11 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
     fence_proxy_async_smem();
   }
   tc_fence_before();
-  __syncthreads();
+  prep_sync<PIPE>();
 
   // 7. U^T = V^T TU^T and W^T = K^T TW^T  (M128 N64 K64; A = V / K^ MN-major, B = TU / TW K-major)
   if (ok && tid == 0) {
-    if (CONV || mbar_wait(bar0 + 8 * B_V, 0, abort_flag)) {
+    if (CONV || mbar_wait(bar0 + 8 * B_V, par, abort_flag)) {
       tc_fence_after();
       constexpr uint32_t ID = idesc_bf16(128, 64, true, false);
 #pragma unroll
@@ -672,7 +679,7 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
       umma_commit(bar0 + 8 * B_MMA2);
     }
   }
-  if (ok) ok = warp_wait(bar0 + 8 * B_MMA2, 0, abort_flag);
+  if (ok) ok = warp_wait(bar0 + 8 * B_MMA2, par, abort_flag);
   // 8. U^T rows (warps 0-3) and W^T rows (warps 4-7) -> workspace, one 128-byte row per thread
   if (ok) {
     tc_fence_after();
@@ -696,14 +703,46 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
   // shared memory are released
   if (tid == 0 && *abort_flag) {
     volatile int never = 0;
-    mbar_wait(bar0 + 8 * B_QK, 0, &never, DRAIN_BUDGET);
-    if (issued_v) mbar_wait(bar0 + 8 * B_V, 0, &never, DRAIN_BUDGET);
+    mbar_wait(bar0 + 8 * B_QK, par, &never, DRAIN_BUDGET);
+    if (issued_v) mbar_wait(bar0 + 8 * B_V, par, &never, DRAIN_BUDGET);
     if (issued_mma) {  // every MMA this thread issued has completed
       umma_commit(bar0 + 8 * B_DRAIN);
       mbar_wait(bar0 + 8 * B_DRAIN, 0, &never, DRAIN_BUDGET);
     }
     atomicOr(&g_delta_error, 1);
   }
+  return *abort_flag == 0;
+}
+
+template <bool CONV>
+__global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
+    const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
+    const __grid_constant__ CUtensorMap mv, const PrepIn in, const int4* __restrict__ info,
+    const int32_t* __restrict__ table, int nseg, int heads, float scale, uint8_t* __restrict__ tiles) {
+  extern __shared__ uint8_t smem_raw[];
+  const int ci = blockIdx.x, h = blockIdx.y;
+  if (ci >= table[nseg]) return;  // CTA-uniform, before any barrier or TMEM use
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* sb = smem_raw + (base - raw);
+  const uint32_t bar0 = base + BARS;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sb + BARS + 8 * NBAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sb + BARS + 8 * NBAR + 4);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  if (tid == 0) {
+    for (int i = 0; i < NBAR; ++i) mbar_init(bar0 + 8 * i, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(tmem_slot), TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  prep_tile<CONV, false>(mq, mk, mv, in, info, heads, scale, tiles, ci, h, base, sb, tmem, 0);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -754,7 +793,31 @@ struct RParams {
   const float* init_state;
   bf16* out;
   float* final_state;
+  const int* tile_ready;  // pipelined launch: per (chunk, head) tile, set once the prep has written it
 };
+
+// Bounded wait until *flag != 0 (acquire), then a proxy fence so the TMA loads that follow see the
+// tile the flag publishes.  Gives up after ~budget SM cycles, raising *abort.
+__device__ __forceinline__ bool wait_tile_ready(const int* flag, volatile int* abort, long long budget = 4000000000LL) {
+  auto ld = [&]() {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];\n" : "=r"(v) : "l"(flag) : "memory");
+    return v;
+  };
+  if (!ld()) {
+    const long long t0 = clock64();
+    for (uint32_t i = 1;; ++i) {
+      if (ld()) break;
+      __nanosleep(64);
+      if ((i & 63) == 0 && (*abort || clock64() - t0 > budget)) {
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+  asm volatile("fence.proxy.async.global;\n" ::: "memory");
+  return true;
+}
 
 struct StageMeta {  // written by the producer before the stage's expect_tx arrive
   int s, h, c, nch;
@@ -768,11 +831,11 @@ struct StageMeta {  // written by the producer before the stage's expect_tx arri
 // row r of S^T, U^T and vn), so a (segment, head) is run as two chains of 64 dv rows each on two
 // CTAs: twice the chains when there are fewer chains than SMs (batch 1 has 16), with M = 64 MMAs
 // (accumulator rows in lanes 0-15 of each TMEM lane quarter) and only that half of U^T loaded.
-template <int SPLIT>
-__global__ void __launch_bounds__(THREADS, 1)
-delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_constant__ CUtensorMap mqg,
-                      const __grid_constant__ CUtensorMap mkg, const __grid_constant__ CUtensorMap ma,
-                      const __grid_constant__ CUtensorMap mut, const RParams p) {
+// PIPE: the tiles are produced during this launch by other CTAs (gdn_pipe_kernel): the producer
+// acquires each tile's ready flag before loading it and reads gamma coherently.
+template <int SPLIT, bool PIPE>
+__device__ __forceinline__ void recur_body(const CUtensorMap& mw, const CUtensorMap& mqg, const CUtensorMap& mkg,
+                                           const CUtensorMap& ma, const CUtensorMap& mut, const RParams& p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -827,12 +890,16 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
           const int st = n & 1;
           if (n >= 2 && !mbar_wait(bar0 + 8 * (B_EMPTY0 + st), ((n >> 1) - 1) & 1, abort_flag)) { ok = false; break; }
           const int z = (c0 + c) * H + h;
+          if constexpr (PIPE) {
+            if (!wait_tile_ready(p.tile_ready + z, abort_flag)) { ok = false; break; }
+          }
           meta[st].s = s;
           meta[st].h = h;
           meta[st].c = c;
           meta[st].nch = nch;
           meta[st].half = half;
-          meta[st].gamma = __ldg(reinterpret_cast<const float*>(p.tiles + (size_t)z * CH_BYTES + OFF_GAMMA));
+          const float* gp = reinterpret_cast<const float*>(p.tiles + (size_t)z * CH_BYTES + OFF_GAMMA);
+          meta[st].gamma = PIPE ? *reinterpret_cast<const volatile float*>(gp) : __ldg(gp);
           const uint32_t sb = base + st * ST_BYTES;
           const uint32_t fb = bar0 + 8 * (B_FULL0 + st);
           mbar_expect_tx(fb, stage_tx);
@@ -1089,6 +1156,14 @@ delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_const
   if (tid == 0 && *abort_flag) atomicOr(&g_delta_error, 1);
 }
 
+template <int SPLIT>
+__global__ void __launch_bounds__(THREADS, 1)
+delta_recur_tc_kernel(const __grid_constant__ CUtensorMap mw, const __grid_constant__ CUtensorMap mqg,
+                      const __grid_constant__ CUtensorMap mkg, const __grid_constant__ CUtensorMap ma,
+                      const __grid_constant__ CUtensorMap mut, const RParams p) {
+  recur_body<SPLIT, false>(mw, mqg, mkg, ma, mut, p);
+}
+
 // Final state of empty segments (their chains never enter the recurrence): the initial state, or 0.
 __global__ void empty_state_kernel(const int32_t* __restrict__ table, int heads, const float* __restrict__ init,
                                    float* __restrict__ fin) {
@@ -1170,6 +1245,88 @@ static int raw_map(CUtensorMap* m, const void* ptr, int64_t tokens, int64_t cols
 
 }  // namespace drtc
 
+// ------------------------------------------------------------------------------------ pipelined
+// Prep and recurrence in ONE launch, for few chains (batch-1 decisions: 16 heads of one request).
+// Two back-to-back launches leave the recurrence waiting for every tile although it needs chunk c
+// only at its c-th step; here they overlap chunk by chunk.  Grid = one CTA per SM (the recurrence's
+// shared memory allows one), so every CTA is resident: CTAs [0, rec_ctas) run the recurrence (two
+// 64-row halves per (segment, head), as delta_recur_tc_kernel<2>); the others take prep tiles in
+// chunk-major order from an atomic counter (tile t = chunk * heads + head) and, once a tile is in
+// the workspace, set its ready flag (release).  The recurrence's producer acquires that flag (a
+// bounded wait) before its TMA loads of the tile.  A tile is only ever waited on after some running
+// CTA has claimed it or will claim it, so every wait has a producer making progress.
+namespace dpipe {
+
+template <bool CONV>
+__global__ void __launch_bounds__(drtc::THREADS, 1)
+gdn_pipe_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
+                const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mw,
+                const __grid_constant__ CUtensorMap mqg, const __grid_constant__ CUtensorMap mkg,
+                const __grid_constant__ CUtensorMap ma, const __grid_constant__ CUtensorMap mut,
+                const dprep::PrepIn in, const int4* __restrict__ info, const int32_t* __restrict__ table, int nseg,
+                int heads, float scale, uint8_t* __restrict__ tiles, const drtc::RParams rp, int rec_ctas,
+                int32_t* __restrict__ ready, int32_t* __restrict__ prep_counter, int n_tiles) {
+  if ((int)blockIdx.x < rec_ctas) {
+    drtc::recur_body<2, true>(mw, mqg, mkg, ma, mut, rp);
+    return;
+  }
+  using namespace dprep;
+  using namespace sm100;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* sb = smem_raw + (base - raw);
+  const uint32_t bar0 = base + BARS;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sb + BARS + 8 * NBAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sb + BARS + 8 * NBAR + 4);
+  volatile int* claim = reinterpret_cast<volatile int*>(sb + BARS + 8 * NBAR + 8);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  if (tid == 0) {
+    for (int i = 0; i < NBAR; ++i) mbar_init(bar0 + 8 * i, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(tmem_slot), TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (warp < THREADS / 32) {  // the 256 prep threads; the other warps wait at the final barrier
+    const int nchunks = table[nseg];
+    for (uint32_t local = 0;; ++local) {
+      if (tid == 0) *claim = atomicAdd(prep_counter, 1);
+      prep_sync<true>();
+      const int t = *claim;  // every thread reads it before the barrier that ends this iteration
+      const int ci = t / heads, h = t - (t / heads) * heads;
+      if (t >= n_tiles || ci >= nchunks) break;  // uniform
+      bool ok = prep_tile<CONV, true>(mq, mk, mv, in, info, heads, scale, tiles, ci, h, base, sb, tmem, local & 1);
+      // the tile's global stores before the flag that publishes them to TMA readers; this tile's
+      // shared-memory writes and TMEM loads before the next tile's TMA writes and MMAs
+      asm volatile("fence.proxy.async.global;\n" ::: "memory");
+      fence_proxy_async_smem();
+      tc_fence_before();
+      ok = prep_sync_and<true>(ok);  // all of the tile's stores are done (and the claim slot was read)
+      tc_fence_after();
+      if (!ok) break;
+      if (tid == 0) {
+        __threadfence();
+        asm volatile("st.release.gpu.global.b32 [%0], %1;\n" ::"l"(ready + t), "r"(1) : "memory");
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TM_COLS);
+  }
+}
+
+}  // namespace dpipe
+
 int delta_take_device_error() {
   int h = 0;
   if (cudaMemcpyFromSymbol(&h, g_delta_error, sizeof(int)) != cudaSuccess) {
@@ -1224,6 +1381,50 @@ extern "C" size_t fdk_chunk_gated_delta_rule_workspace_size(int64_t tokens, int6
 
 // Table, prep (plain or with the fused conv + gate prologue) and recurrence.  `q / k / v` are used
 // by the plain prep only; the caller has validated everything.
+static int run_pipelined(bool conv, const void* q, const void* k, int64_t ld_qk, const void* v, int64_t ld_v,
+                         const dprep::PrepIn& in, const WsLayout& lay, const int32_t* cu, int nseg, int64_t tokens,
+                         int64_t heads, float scale, const float* init, bf16* out, float* fin, uint8_t* ws,
+                         cudaStream_t s) {
+  int32_t* table = reinterpret_cast<int32_t*>(ws + lay.off_table);
+  const int4* info = reinterpret_cast<const int4*>(ws + lay.off_info);
+  uint8_t* tiles = ws + lay.off_tiles;
+  int32_t* ready = reinterpret_cast<int32_t*>(ws + lay.off_ready);
+  const int64_t n_tiles = lay.max_chunks * heads;
+  if (fin) {
+    drtc::empty_state_kernel<<<dim3((unsigned)nseg, (unsigned)heads), 256, 0, s>>>(table, (int)heads, init, fin);
+    if (int st = check_launch("chunk_gated_delta_rule/empty segments")) return st;
+  }
+  CUtensorMap mq, mk, mv, mw, mqg, mkg, ma, mut;
+  if (conv) {
+    memset(&mk, 0, sizeof(mk));
+    memset(&mv, 0, sizeof(mv));
+    if (int st = drtc::raw_map(&mq, in.proj, tokens, 3 * (int64_t)in.key_dim, in.ld)) return st;
+  } else {
+    if (int st = drtc::act_map(&mq, q, tokens, heads, ld_qk)) return st;
+    if (int st = drtc::act_map(&mk, k, tokens, heads, ld_qk)) return st;
+    if (int st = drtc::act_map(&mv, v, tokens, heads, ld_v)) return st;
+  }
+  if (int st = drtc::tile_map(&mw, tiles, OFF_W, DR_C, DR_D, n_tiles)) return st;
+  if (int st = drtc::tile_map(&mqg, tiles, OFF_QG, DR_D, DR_C, n_tiles)) return st;
+  if (int st = drtc::tile_map(&mkg, tiles, OFF_KG, DR_D, DR_C, n_tiles)) return st;
+  if (int st = drtc::tile_map(&ma, tiles, OFF_A, DR_C, DR_C, n_tiles)) return st;
+  if (int st = drtc::tile_map(&mut, tiles, OFF_UT, DR_C, DR_D, n_tiles, DR_D / 2)) return st;
+  drtc::RParams rp{cu, table, table + nseg + 1, nseg, (int)heads, tiles, init, out, fin, ready};
+  const void* fn = conv ? (const void*)dpipe::gdn_pipe_kernel<true> : (const void*)dpipe::gdn_pipe_kernel<false>;
+  if (int st = ensure_smem_attr(fn, (int)drtc::SMEM_BYTES, "chunk_gated_delta_rule/pipelined")) return st;
+  const int rec_ctas = (int)(2 * (int64_t)nseg * heads);
+  const unsigned grid = (unsigned)sm_count();
+  if (conv)
+    dpipe::gdn_pipe_kernel<true><<<grid, drtc::THREADS, drtc::SMEM_BYTES, s>>>(
+        mq, mk, mv, mw, mqg, mkg, ma, mut, in, info, table, nseg, (int)heads, scale, tiles, rp, rec_ctas, ready,
+        table + nseg + 2, (int)n_tiles);
+  else
+    dpipe::gdn_pipe_kernel<false><<<grid, drtc::THREADS, drtc::SMEM_BYTES, s>>>(
+        mq, mk, mv, mw, mqg, mkg, ma, mut, in, info, table, nseg, (int)heads, scale, tiles, rp, rec_ctas, ready,
+        table + nseg + 2, (int)n_tiles);
+  return check_launch("chunk_gated_delta_rule/pipelined");
+}
+
 static int run_delta_rule(bool conv, const void* q, const void* k, int64_t ld_qk, const void* v, int64_t ld_v,
                           const dprep::PrepIn& in, const int32_t* cu_seqlens, int64_t num_segments, int64_t tokens,
                           int64_t heads, float scale, const float* initial_state, void* out, float* final_state,
@@ -1237,9 +1438,20 @@ static int run_delta_rule(bool conv, const void* q, const void* k, int64_t ld_qk
   int4* info = reinterpret_cast<int4*>(ws + lay.off_info);
   uint8_t* tiles = ws + lay.off_tiles;
   const int nseg = (int)num_segments;
-  chunk_table_kernel<<<1, 256, 0, s>>>(cu_seqlens, nseg, tokens, lay.max_chunks, table, info);
+  int32_t* ready = reinterpret_cast<int32_t*>(ws + lay.off_ready);
+  chunk_table_kernel<<<1, 256, 0, s>>>(cu_seqlens, nseg, tokens, lay.max_chunks, table, info, ready,
+                                       lay.max_chunks * heads);
   if (int st = check_launch("chunk_gated_delta_rule/table")) return st;
   if (tokens == 0 && !final_state) return FDK_OK;
+  // One request (batch-1 decisions) with few heads: prep and recurrence pipelined in one launch (at
+  // most half the SMs run chains, at least as many make tiles).  Measured: config 4 (1536 tokens, 16
+  // heads) 85 -> 76 us, one 8192-token request ~390 -> 264 us; with two or more requests the prep,
+  // one tile at a time per SM here (each tile ~16 us of latency), becomes the bound and the two
+  // launches are faster.
+  const int64_t chains = num_segments * heads;
+  if (tokens > 0 && num_segments == 1 && 4 * chains <= sm_count())
+    return run_pipelined(conv, q, k, ld_qk, v, ld_v, in, lay, cu_seqlens, nseg, tokens, heads, scale, initial_state,
+                         static_cast<bf16*>(out), final_state, ws, s);
   if (tokens > 0) {
     CUtensorMap mq, mk, mv;
     if (conv) {  // the fused prologue reads the projection through one map (passed as mq)

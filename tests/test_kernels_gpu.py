@@ -306,6 +306,11 @@ def test_delta_rule_exact_chunks_and_tail():
     delta_check(1, 2, 4)
 
 
+def test_delta_rule_single_request_initial_state():
+    # one request: prep and recurrence pipelined in one launch; initial and final states
+    delta_check(700, 8, 12, init=True)
+
+
 def test_delta_rule_varlen_segments():
     delta_check(300, 4, 5, cu=[0, 1, 64, 65, 129, 200, 200, 300])
 
