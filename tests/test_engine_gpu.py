@@ -214,3 +214,28 @@ def test_reference_attention_geometry_8q_2kv_d256():
     err_base = (base[0].float().cpu() - ref).abs()
     assert err_ours.mean().item() <= 1.5 * err_base.mean().item() + 1e-3
     assert err_ours.max().item() <= 2.0 * err_base.max().item() + 2e-2
+
+
+def test_bucketed_graphs_match_eager(cfg, weights):
+    """Small batches through their bucket's CUDA graph (padded up to the bucket, the padding as one
+    extra segment) give the eager forward's probabilities; after seal() an uncaptured bucket runs
+    eagerly instead of capturing."""
+    from fastdecisions_b200.engine import pack
+    eng = DecisionEngine(cfg, weights, "cuda")
+    reqs = requests(cfg, ((70, 2), (150, 8), (33, 4), (1, 3)), seed=21)
+    b = pack(reqs)
+    (ids, cu, pos, slots, nopts), _ = eng.to_device(b)
+    eager, _ = eng.forward_device(ids, cu, pos, slots, nopts, b.max_seqlen)
+    first = eng.forward_graphed(b).cpu().numpy()     # captures the bucket (padded to 256 tokens)
+    again = eng.forward_graphed(b).cpu().numpy()     # replays it
+    assert eng.stats["graph_captures"] == 1 and eng.stats["graph_replays"] == 2
+    assert np.abs(first - eager.cpu().numpy()).max() < 2e-3 and np.abs(again - first).max() == 0
+    one = requests(cfg, ((300, 5),), seed=22)         # score(graphs=True) graphs single requests
+    g1 = eng.score(one, graphs=True)
+    assert eng.stats["graph_captures"] == 2
+    assert np.abs(g1 - eng.score(one)).max() < 2e-3
+    eng.seal()
+    big = requests(cfg, ((2500, 4),), seed=23)        # a bucket not captured yet: eager after seal()
+    captures = eng.stats["graph_captures"]
+    assert np.abs(eng.score(big, graphs=True) - eng.score(big)).max() == 0
+    assert eng.stats["graph_captures"] == captures
