@@ -201,7 +201,7 @@ def delta_rule_flops(batch, cfg) -> float:
     return cfg.linear_num_value_heads * float(np.ceil(L / 64).sum()) * 11.7e6
 
 
-def op_work(cfg, batches, fused_swiglu=True, fused_qkv=True) -> dict:
+def op_work(cfg, batches, fused_swiglu=True, fused_qkv=True, fused_residual=True) -> dict:
     """Algorithmic work of one step per op type: ("tensor", FLOPs) or ("hbm", bytes).  Bytes count
     each input read once and each output written once (bf16 activations, fp32 residual stream)."""
     n_att = sum(1 for t in cfg.layer_types if t == "full_attention")
@@ -218,8 +218,14 @@ def op_work(cfg, batches, fused_swiglu=True, fused_qkv=True) -> dict:
     T_qkv = float(sum(b.tokens for b in batches if b.tokens >= FUSED_QKV_MIN_TOKENS)) if fused_qkv else 0.0
     gate_up = cfg.num_hidden_layers * 2.0 * H * 2 * I * T_fused  # MLP gate/up GEMMs run SwiGLU-fused
     qkv = n_att * 2.0 * H * (2 * hq + 2 * hkv) * D * T_qkv       # attention projections with q/k norm fused
+    # out-projections and MLP down-projections adding into the fp32 residual stream
+    from fastdecisions_b200.engine import FUSED_RESIDUAL_MIN_TOKENS
+    T_res = float(sum(b.tokens for b in batches if b.tokens >= FUSED_RESIDUAL_MIN_TOKENS)) if fused_residual else 0.0
+    resadd = (n_lin * 2.0 * vd * H + n_att * 2.0 * hq * D * H + cfg.num_hidden_layers * 2.0 * I * H) * T_res
+    # a layer norm moves h read (+ x read, h write) and out: 6 bytes an element after a residual-add GEMM
     w = {
-        "gemm": ("tensor", 2.0 * cfg.linear_params() * T - gate_up - qkv),  # cuBLAS projections
+        "gemm": ("tensor", 2.0 * cfg.linear_params() * T - gate_up - qkv - resadd),  # cuBLAS projections
+        "gemm_residual_add": ("tensor", resadd),                             # own GEMM adding into the stream
         "gemm_swiglu": ("tensor", gate_up),                                  # own tcgen05 GEMM + SwiGLU epilogue
         "gemm_qk_norm_rope": ("tensor", qkv),                                # own tcgen05 GEMM + q/k norm, RoPE
         "gqa_attention": ("tensor", n_att * sum(attention_flops(b, cfg) for b in batches)),
@@ -229,7 +235,8 @@ def op_work(cfg, batches, fused_swiglu=True, fused_qkv=True) -> dict:
         "gated_rmsnorm": ("hbm", n_lin * T * vd * (2 + 2 + 2)),
         "qk_norm_rope": ("hbm", n_att * (T - T_qkv) * (hq + hkv) * D * 2 * 2),
         # x (bf16) + residual (fp32) read, residual (fp32) + normed (bf16) written
-        "residual_rmsnorm": ("hbm", (2 * cfg.num_hidden_layers - 1) * T * H * (2 + 4 + 4 + 2) + T * H * (2 + 4 + 2)),
+        "residual_rmsnorm": ("hbm", (2 * cfg.num_hidden_layers - 1) * H * (T_res * 6 + (T - T_res) * 12)
+                             + T * H * (2 + 4 + 2)),
         "swiglu": ("hbm", cfg.num_hidden_layers * (T - T_fused) * I * (2 * 2 + 2)),  # batches not fused
         "embed": ("hbm", T * H * 2 * 2),
         "slot_readout": ("hbm", S * H * (4 + 2)),
@@ -425,7 +432,8 @@ def run_ours(args, world, rank, local):
     cfg = W.ModelConfig()
     threads = max(1, (os.cpu_count() or 1) // max(1, world))
     weights = W.synthetic_weights(cfg, threads=threads)
-    engine = DecisionEngine(cfg, weights, dev, fused_swiglu_gemm=not args.cublas_mlp, fused_qkv_gemm=args.fused_qkv)
+    engine = DecisionEngine(cfg, weights, dev, fused_swiglu_gemm=not args.cublas_mlp, fused_qkv_gemm=args.fused_qkv,
+                            fused_residual_gemm=not args.cublas_residual)
     timer = KernelTimer()
     engine.kernel_timer = timer
 
@@ -499,7 +507,8 @@ def run_ours(args, world, rank, local):
     timer.enabled = False
     tot = timer.totals()
     pk, pk_kind = peaks()
-    work = op_work(cfg, batches, engine.fused_swiglu_gemm, engine.fused_qkv_gemm)  # per step: {op: (bound, units)}
+    work = op_work(cfg, batches, engine.fused_swiglu_gemm, engine.fused_qkv_gemm,
+                   engine.fused_residual_gemm)  # per step: {op: (bound, units)}
     roof = {}
     for name, (bound, units) in work.items():
         if name not in tot or tot[name]["total_ms"] <= 0:
@@ -660,6 +669,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=25.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--streams", type=int, default=2, help="CUDA streams the packed batches are spread over")
+    ap.add_argument("--cublas-residual", action="store_true",
+                    help="out / down projections on cuBLAS with the separate residual add + RMSNorm kernel")
     ap.add_argument("--fused-qkv", action="store_true",
                     help="attention projection as the tcgen05 GEMM with q/k norm + RoPE fused (default: cuBLAS + "
                          "the separate kernel, measured faster)")

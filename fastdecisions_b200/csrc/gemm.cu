@@ -31,14 +31,15 @@ constexpr uint32_t A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, ST_BYTES = A_BY
 constexpr uint32_t OUT_BOX = 32 * 128;                     // [32 rows][64 bf16] output block, 128-byte swizzle
 constexpr uint32_t OFF_OUT = STAGES * ST_BYTES;              // per epilogue warp: two OUT_BOX buffers
 constexpr uint32_t OFF_BAR = OFF_OUT + 4 * 2 * OUT_BOX;
+constexpr int UNIT_RING = 16;  // claimed work units in flight between the producer and the consumers
 enum { B_FULL = 0, B_EMPTY = STAGES, B_TFULL = 2 * STAGES, B_TEMPTY = 2 * STAGES + 2, B_DRAIN = 2 * STAGES + 4,
-       NBAR = 2 * STAGES + 5 };
-constexpr uint32_t SMEM_BYTES = OFF_BAR + 8 * NBAR + 16 + 1024;
+       B_UNIT = 2 * STAGES + 5, NBAR = 2 * STAGES + 5 + UNIT_RING };
+constexpr uint32_t SMEM_BYTES = OFF_BAR + 8 * NBAR + 16 + 4 * UNIT_RING + 1024;
 constexpr int THREADS = 192;
 constexpr uint32_t TM_COLS = 512;
 constexpr long long DRAIN_BUDGET = 2000000000LL;
 
-enum Epi { PLAIN = 0, SWIGLU = 1, QKNORM128 = 2, QKNORM256 = 3 };
+enum Epi { PLAIN = 0, SWIGLU = 1, QKNORM128 = 2, QKNORM256 = 3, RESADD = 4 };
 
 __device__ int g_gemm_error = 0;
 
@@ -54,9 +55,20 @@ struct Params {
   int max_pos;
   float eps;
   int band;             // n-blocks per band of the tile order
+  int k_split, kps;     // work unit = (tile, one of k_split slices of kps k-steps); RESADD only splits
+  int* tickets;         // RESADD with k_split > 1: [tiles][4] slice tickets, then the claim and exit
+                        // counters of the dynamic schedule (all zero between calls)
+  int dynamic;          // units claimed from tickets[4 tiles] instead of the static round robin
   bf16* c;
   int64_t ldc;
 };
+
+// work unit -> (tile, first k-step, k-steps); the slices of one tile are consecutive units
+__device__ __forceinline__ void unit_coords(int u, const Params& p, int& t, int& ks0, int& nks) {
+  t = u / p.k_split;
+  ks0 = (u - t * p.k_split) * p.kps;
+  nks = min(p.kps, p.k_steps - ks0);
+}
 
 // tile index -> (m block, n block): bands of p.band n-blocks, n fastest inside a band (the ~148
 // tiles in flight share a few A row blocks and the band's B blocks in L2)
@@ -80,10 +92,26 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
   const uint32_t bar0 = base + OFF_BAR;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + OFF_BAR + 8 * NBAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_BAR + 8 * NBAR + 4);
+  volatile int* unit_ring = reinterpret_cast<volatile int*>(gbase + OFF_BAR + 8 * NBAR + 16);
   auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int num_tiles = p.m_tiles * p.n_tiles;
-
+  const int num_units = p.m_tiles * p.n_tiles * p.k_split;
+  int* claim = p.dynamic ? p.tickets + 4 * p.m_tiles * p.n_tiles : nullptr;  // then the exit counter
+  // The unit of this CTA's local-th turn, -1 when there is none left.  Static: round robin.
+  // Dynamic (ordered split-K): the producer claims units from an atomic counter and publishes them
+  // in a ring with one mbarrier an entry; a claimed unit's earlier slices were claimed before it,
+  // by CTAs that are running, so every ticket wait has a running producer.  The ring cannot be
+  // overrun: the producer is at most STAGES k-steps (units) ahead of the MMAs, which are at most
+  // two units ahead of the epilogue.
+  auto consumer_unit = [&](int local, bool& ok) -> int {
+    if (!p.dynamic) {
+      const int u = blockIdx.x + local * gridDim.x;
+      return u < num_units ? u : -1;
+    }
+    const int e = local % UNIT_RING;
+    ok = mbar_wait(bar(B_UNIT + e), (local / UNIT_RING) & 1, abort_flag);
+    return ok ? unit_ring[e] : -1;
+  };
   if (tid == 0) {
     for (int i = 0; i < NBAR; ++i) mbar_init(bar(i), (i == B_TEMPTY || i == B_TEMPTY + 1) ? 128u : 1u);
     *abort_flag = 0;
@@ -105,10 +133,22 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
       prefetch_tmap(&tb);
       int it = 0;  // k-steps issued by this CTA (ring position)
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
-        int mb, nb;
+      for (int local = 0; ok; ++local) {
+        int u;
+        if (p.dynamic) {
+          u = atomicAdd(claim, 1);
+          if (u >= num_units) u = -1;
+          unit_ring[local % UNIT_RING] = u;
+          mbar_arrive(bar(B_UNIT + local % UNIT_RING));
+        } else {
+          u = blockIdx.x + local * gridDim.x;
+          if (u >= num_units) u = -1;
+        }
+        if (u < 0) break;
+        int t, ks0, nks, mb, nb;
+        unit_coords(u, p, t, ks0, nks);
         tile_coords(t, p, mb, nb);
-        for (int ks = 0; ks < p.k_steps; ++ks, ++it) {
+        for (int ks = ks0; ks < ks0 + nks; ++ks, ++it) {
           const int st = it % STAGES;
           if (it >= STAGES && !mbar_wait(bar(B_EMPTY + st), ((it / STAGES) - 1) & 1, abort_flag)) {
             ok = false;
@@ -131,13 +171,17 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
       constexpr uint32_t IDESC = idesc_bf16(BM, BN, false, false);
       int it = 0, local = 0;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x, ++local) {
+      for (; ok; ++local) {
+        const int u = consumer_unit(local, ok);
+        if (u < 0) break;
+        int t, ks0, nks;
+        unit_coords(u, p, t, ks0, nks);
         const int acc = local & 1;
         // the epilogue has drained this accumulator (its previous use was tile local - 2)
         if (local >= 2 && !mbar_wait(bar(B_TEMPTY + acc), ((local >> 1) - 1) & 1, abort_flag)) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)acc * BN;
-        for (int ks = 0; ks < p.k_steps; ++ks, ++it) {
+        for (int ks = ks0; ks < ks0 + nks; ++ks, ++it) {
           const int st = it % STAGES;
           if (!mbar_wait(bar(B_FULL + st), (it / STAGES) & 1, abort_flag)) {
             ok = false;
@@ -148,7 +192,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
           const uint64_t da = sdesc_sw128(sa, 16, 1024), db = sdesc_sw128(sa + A_BYTES, 16, 1024);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
-            umma_ss(d, da + (uint32_t)(2 * kk), db + (uint32_t)(2 * kk), IDESC, (ks > 0 || kk > 0) ? 1u : 0u);
+            umma_ss(d, da + (uint32_t)(2 * kk), db + (uint32_t)(2 * kk), IDESC, (ks > ks0 || kk > 0) ? 1u : 0u);
           umma_commit(bar(B_EMPTY + st));
         }
         if (ok) umma_commit(bar(B_TFULL + acc));
@@ -188,11 +232,15 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
       }
       ++pieces;
     };
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+    for (;; ++local) {
+      bool uok = true;
+      const int u = __shfl_sync(0xffffffffu, consumer_unit(local, uok), 0);
+      if (u < 0) break;
       const int acc = local & 1;
       if (!__all_sync(0xffffffffu, mbar_wait(bar(B_TFULL + acc), (local >> 1) & 1, abort_flag) ? 1 : 0)) break;
       tc_fence_after();
-      int mb, nb;
+      int t, ks0, nks, mb, nb;
+      unit_coords(u, p, t, ks0, nks);
       tile_coords(t, p, mb, nb);
       const int y = mb * BM + q4 * 32;
       const uint32_t tacc = tmem + lane_addr + (uint32_t)acc * BN;
@@ -212,6 +260,64 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
           for (int i = 0; i < 64; ++i) f[i] = __uint_as_float(v[i >> 5][i & 31]);
           put_piece(f, &tc, nb * BN + c * 64, y);
         }
+      } else if constexpr (EPI == RESADD) {
+        // C (fp32) += acc: 32-column pieces staged as [32 rows][32 fp32] (128-byte rows, swizzled)
+        // and added by TMA reduce-add stores, so the k-slices of a tile sum in place.  The slices add
+        // in a fixed order (slice 0 first): this warp's rows wait on their ticket until the previous
+        // slice's adds have completed, so results do not depend on scheduling.
+        const int slice = u - t * p.k_split;
+        int* ticket = p.k_split > 1 ? p.tickets + (int64_t)t * 4 + q4 : nullptr;
+        if (ticket != nullptr && slice > 0) {
+          bool ok = true;
+          if (lane == 0) {
+            const long long t0 = clock64();
+            for (uint32_t i = 0;; ++i) {
+              int v;
+              asm volatile("ld.acquire.gpu.global.b32 %0, [%1];\n" : "=r"(v) : "l"(ticket) : "memory");
+              if (v == slice) break;
+              if ((i & 63) == 63 && (*abort_flag || clock64() - t0 > 4000000000LL)) {
+                *abort_flag = 1;
+                ok = false;
+                break;
+              }
+              __nanosleep(32);
+            }
+            asm volatile("fence.proxy.async.global;\n" ::: "memory");
+          }
+          if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+        }
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tacc + c * 32, v);
+          tmem_ld_wait();
+          if (c == BN / 32 - 1) {
+            tc_fence_before();
+            mbar_arrive(bar(B_TEMPTY + acc));
+          }
+          const int b = pieces & 1;
+          if (lane == 0 && pieces >= 2) bulk_wait_read<1>();
+          __syncwarp();
+          uint8_t* dst = obuf_g + b * OUT_BOX + lane * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<uint4*>(dst + ((j ^ (lane & 7)) << 4)) = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_reduce_add_2d(&tc, obuf + b * OUT_BOX, nb * BN + c * 32, y);
+            bulk_commit();
+          }
+          ++pieces;
+        }
+        if (ticket != nullptr && lane == 0) {  // this slice's adds are done: pass the ticket on
+          bulk_wait<0>();
+          asm volatile("fence.proxy.async.global;\n" ::: "memory");
+          __threadfence();
+          const int next = slice + 1 == p.k_split ? 0 : slice + 1;  // the last slice leaves it zeroed
+          asm volatile("st.release.gpu.global.b32 [%0], %1;\n" ::"l"(ticket), "r"(next) : "memory");
+        }
+        __syncwarp();
       } else if constexpr (EPI == SWIGLU) {
 #pragma unroll 1
         for (int c = 0; c < BN / 128; ++c) {
@@ -321,6 +427,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
     tmem_dealloc(tmem, TM_COLS);
   }
   if (tid == 0 && *abort_flag) atomicOr(&g_gemm_error, 1);
+  if (tid == 0 && p.dynamic) {  // the last CTA out leaves both counters zeroed for the next call
+    __threadfence();
+    if (atomicAdd(claim + 1, 1) == (int)gridDim.x - 1) {
+      claim[0] = 0;
+      claim[1] = 0;
+      __threadfence();
+    }
+  }
 }
 
 using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
@@ -350,6 +464,20 @@ static int kmajor_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t col
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(FDK_ERR_INVALID_ARGUMENT, "gemm: tensor map encode failed (%d)", (int)r);
+  return FDK_OK;
+}
+
+// [rows][cols] float32 (row stride ld elements), box 32 x box_rows, 128-byte swizzle
+static int f32_map(CUtensorMap* m, void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  EncodeFn enc = encode_fn();
+  if (!enc) return set_error(FDK_ERR_DEVICE, "gemm: cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+  cuuint32_t box[2] = {32, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(FDK_ERR_INVALID_ARGUMENT, "gemm: tensor map encode failed (%d)", (int)r);
   return FDK_OK;
 }
@@ -403,6 +531,8 @@ extern "C" int fdk_gemm_bf16(const void* a, int64_t lda, const void* b, int64_t 
   p.n_tiles = (int)((n + BN - 1) / BN);
   p.k_steps = (int)((k + BK - 1) / BK);
   p.band = 8;  // measured: sweeping every n-block first (A read from HBM once) was no faster
+  p.k_split = 1;
+  p.kps = p.k_steps;
   p.c = static_cast<bf16*>(c);
   p.ldc = ldc;
   const int64_t tiles = (int64_t)p.m_tiles * p.n_tiles;
@@ -458,6 +588,8 @@ extern "C" int fdk_gemm_bf16_qk_norm_rope(const void* a, int64_t lda, const void
   p.n_tiles = (int)((n + BN - 1) / BN);
   p.k_steps = (int)((k + BK - 1) / BK);
   p.band = 8;
+  p.k_split = 1;
+  p.kps = p.k_steps;
   p.c = static_cast<bf16*>(c);
   p.ldc = ldc;
   p.hq = (int)hq;
@@ -480,4 +612,50 @@ extern "C" int fdk_gemm_bf16_qk_norm_rope(const void* a, int64_t lda, const void
     gemm_kernel<QKNORM256><<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, mc, mq, mk, p);
   }
   return check_launch("gemm_qk_norm_rope");
+}
+
+extern "C" int fdk_gemm_bf16_residual_add(const void* a, int64_t lda, const void* b, int64_t ldb, float* h, int64_t ldh,
+                                          int64_t m, int64_t n, int64_t k, int split_k, int32_t* tickets,
+                                          void* stream) {
+  using namespace fdk::gemm;
+  if (int st = check_device()) return st;
+  if (!a || !b || !h) return set_error(FDK_ERR_INVALID_ARGUMENT, "gemm_residual_add: null pointer");
+  if (m < 0 || n <= 0 || k <= 0 || m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff)
+    return set_error(FDK_ERR_INVALID_ARGUMENT, "gemm_residual_add: bad sizes");
+  if (split_k < 0 || split_k > 16) return set_error(FDK_ERR_INVALID_ARGUMENT, "gemm_residual_add: split_k in [0, 16]");
+  if (n % 8 || k % 8) return set_error(FDK_ERR_ALIGNMENT, "gemm_residual_add: n and k must be multiples of 8");
+  if (lda < k || ldb < k || ldh < n) return set_error(FDK_ERR_INVALID_ARGUMENT, "gemm_residual_add: row stride too small");
+  if (!aligned16(a) || !aligned16(b) || !aligned16(h) || lda % 8 || ldb % 8 || ldh % 4)
+    return set_error(FDK_ERR_ALIGNMENT, "gemm_residual_add: pointers and row strides must be 16-byte aligned");
+  if (m == 0) return FDK_OK;
+  CUtensorMap ma, mb, mh;
+  if (int st = kmajor_map(&ma, a, m, k, lda, BM)) return st;
+  if (int st = kmajor_map(&mb, b, n, k, ldb, BN)) return st;
+  if (int st = f32_map(&mh, h, m, n, ldh, 32)) return st;  // [32 rows][32 fp32] boxes
+  Params p{};
+  p.m = (int)m;
+  p.n = (int)n;
+  p.k = (int)k;
+  p.m_tiles = (int)((m + BM - 1) / BM);
+  p.n_tiles = (int)((n + BN - 1) / BN);
+  p.k_steps = (int)((k + BK - 1) / BK);
+  p.band = 8;
+  const int64_t tiles = (int64_t)p.m_tiles * p.n_tiles;
+  if (tiles * 16 > 0x7fffffff) return set_error(FDK_ERR_UNSUPPORTED, "gemm_residual_add: too many tiles");
+  // 0 = no split: ordered slices serialise their epilogues, measured slower than one slice at
+  // m = 1536 (config-4 forward 5.46 ms unsplit, 5.97 with 2 slices, 6.19 with 3)
+  int s = split_k > 0 ? split_k : 1;
+  if (s > p.k_steps) s = p.k_steps;
+  if (tickets == nullptr) s = 1;  // ordered slices need the caller's ticket array
+  p.kps = (p.k_steps + s - 1) / s;
+  p.k_split = (p.k_steps + p.kps - 1) / p.kps;  // every slice non-empty
+  p.c = nullptr;
+  p.ldc = ldh;
+  p.tickets = p.k_split > 1 ? tickets : nullptr;
+  p.dynamic = p.k_split > 1 ? 1 : 0;
+  const int64_t units = tiles * p.k_split;
+  const int grid = (int)(units < sm_count() ? units : sm_count());
+  if (int st = ensure_smem_attr((const void*)gemm_kernel<RESADD>, (int)SMEM_BYTES, "gemm_residual_add")) return st;
+  gemm_kernel<RESADD><<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ma, mb, mh, mh, mh, p);
+  return check_launch("gemm_residual_add");
 }

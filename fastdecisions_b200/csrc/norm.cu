@@ -52,7 +52,12 @@ __global__ void __launch_bounds__(128) residual_rmsnorm_kernel(
   for (int c = 0; c < NC; ++c) {
     const int i = threadIdx.x + c * 128;
     if (i < nvec) {
-      unpack8(ldg_stream(xr + i * 8), v[c]);
+      if (x != nullptr) {
+        unpack8(ldg_stream(xr + i * 8), v[c]);
+      } else {  // the norm of the residual stream alone (its producer already added into it)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[c][j] = 0.f;
+      }
       if (HAS_RES) {
         float r8[8];
         IO::load(res + row * ldr + i * 8, r8);
@@ -258,12 +263,12 @@ extern "C" int fdk_residual_rmsnorm(const void* x, int64_t ld_x, const void* res
                                     int64_t ld_out, void* residual_out, int64_t ld_residual_out, int64_t rows,
                                     int64_t hidden, float eps, float weight_offset, void* stream) {
   if (int st = check_device()) return st;
-  if (!x || !weight || !out) return set_error(FDK_ERR_INVALID_ARGUMENT, "residual_rmsnorm: null pointer");
+  if ((!x && !residual) || !weight || !out) return set_error(FDK_ERR_INVALID_ARGUMENT, "residual_rmsnorm: null pointer");
   if (rows < 0 || hidden <= 0 || hidden % 8 != 0 || hidden > 8192)
     return set_error(FDK_ERR_UNSUPPORTED, "residual_rmsnorm: hidden=%lld must be a positive multiple of 8 <= 8192", (long long)hidden);
-  if (ld_x < hidden || ld_out < hidden || (residual && ld_residual < hidden) || (residual_out && ld_residual_out < hidden))
+  if ((x && ld_x < hidden) || ld_out < hidden || (residual && ld_residual < hidden) || (residual_out && ld_residual_out < hidden))
     return set_error(FDK_ERR_INVALID_ARGUMENT, "residual_rmsnorm: row stride smaller than hidden");
-  if (!aligned16(x) || !aligned16(out) || (residual && !aligned16(residual)) || (residual_out && !aligned16(residual_out)) ||
+  if ((x && !aligned16(x)) || !aligned16(out) || (residual && !aligned16(residual)) || (residual_out && !aligned16(residual_out)) ||
       !aligned16(weight) || ld_x % 8 || ld_out % 8 || (residual && ld_residual % 8) || (residual_out && ld_residual_out % 8))
     return set_error(FDK_ERR_ALIGNMENT, "residual_rmsnorm: pointers and row strides must be 16-byte aligned");
   if (rows == 0) return FDK_OK;

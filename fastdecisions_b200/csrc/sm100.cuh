@@ -72,6 +72,12 @@ __device__ __forceinline__ void tma_store_2d(const void* map, uint32_t src, int 
                "r"(x), "r"(y)
                : "memory");
 }
+// TMA tiled reduce-add from shared memory into global memory (element type from the tensor map)
+__device__ __forceinline__ void tma_reduce_add_2d(const void* map, uint32_t src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];\n" ::"l"(map),
+               "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
 // waits until at most N committed bulk groups of this thread still read their shared-memory source
 template <int N>

@@ -23,7 +23,7 @@ from .engine import plan_batches
 from .workloads import ModelConfig, config5_requests
 
 CUBLAS = False  # --cublas: time torch.matmul (cuBLAS) for the gemm_* ops instead of the own GEMM
-OPS = ("gemm_qkv_norm_rope", "gemm_gdn_in", "gemm_attn_qkv", "gemm_out", "gemm_down", "gemm_gate_up", "gemm_swiglu", "gdn_fused", "delta_rule", "gqa_attention", "packed_conv", "qk_norm_rope", "gated_rmsnorm", "residual_rmsnorm",
+OPS = ("resadd_out", "resadd_down", "gemm_qkv_norm_rope", "gemm_gdn_in", "gemm_attn_qkv", "gemm_out", "gemm_down", "gemm_gate_up", "gemm_swiglu", "gdn_fused", "delta_rule", "gqa_attention", "packed_conv", "qk_norm_rope", "gated_rmsnorm", "residual_rmsnorm",
        "swiglu", "gdn_gates")
 
 
@@ -60,6 +60,17 @@ def make_case(op: str, lens: list, cfg: ModelConfig, seed: int = 0):
     kd, vd = Hk * Dk, Hv * Dv
     C = 2 * kd + vd
     hq, hkv, D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+    if op in ("resadd_out", "resadd_down"):  # the projection into the residual stream + the next norm
+        H, I = cfg.hidden_size, cfg.intermediate_size
+        k = vd if op == "resadd_out" else I
+        a, w = rn(T, k), rn(H, k, scale=0.02)
+        h = torch.randn(T, H, generator=g, device=dev)
+        nw = rn(H, scale=0.02)
+        flops = 2.0 * T * H * k
+        if CUBLAS:  # cuBLAS GEMM (bf16 out), then the fused residual add + RMSNorm
+            return (lambda: ops.residual_rmsnorm(torch.matmul(a, w.t()), h, nw, cfg.rms_norm_eps, residual_out=h)), \
+                ("tensor", flops)
+        return (lambda: ops.rmsnorm_stream(ops.gemm_residual_add(a, w, h), nw, cfg.rms_norm_eps)), ("tensor", flops)
     if op.startswith("gemm_"):  # own tcgen05 GEMM ("gemm_*") or, with --cublas, torch.matmul (cuBLAS)
         H, I = cfg.hidden_size, cfg.intermediate_size
         n, k = {"gemm_gdn_in": (C + vd + 2 * Hv, H), "gemm_attn_qkv": ((2 * hq + 2 * hkv) * D, H),
@@ -185,6 +196,36 @@ def time_rotating(fns, passes: int, warmup: int) -> float:
     return ms
 
 
+def forward_cfg4(replays: int, **engine_opts) -> None:
+    """Config 4 (batch 1, 1536 tokens) through the engine's CUDA graph: ``replays`` replays inside
+    an NVTX range named ``replay`` (profilers select the graph's kernels by it), p50 printed."""
+    import statistics
+    from .engine import DecisionEngine, pack
+    from .workloads import config4_request, synthetic_weights
+    cfg = ModelConfig()
+    split = engine_opts.pop("residual_split_k", 0)
+    eng = DecisionEngine(cfg, synthetic_weights(cfg), "cuda", **engine_opts)
+    eng.residual_split_k = split
+    b = pack([config4_request()])
+    key = eng.capture(b.tokens, 1, b.max_seqlen)
+    d, _ = eng.to_device(b)
+    eng.replay(key, *d)
+    torch.cuda.synchronize()
+    times = []
+    torch.cuda.nvtx.range_push("replay")
+    for _ in range(replays):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        eng.replay(key)
+        e1.record()
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    torch.cuda.nvtx.range_pop()
+    print(json.dumps({"op": "forward_cfg4 (graph replay)", "tokens": b.tokens, "replays": replays, "opts": engine_opts,
+                      "residual_split_k": split,
+                      "p50_ms": round(statistics.median(times), 4), "min_ms": round(min(times), 4)}), flush=True)
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--op", default="all", help="one of %s, or all" % ", ".join(OPS))
@@ -200,7 +241,12 @@ def main(argv=None):
     ap.add_argument("--attn", default=None,
                     help="attention geometry hq,hkv,head_dim (e.g. 8,2,256: the reference kernel's own shape)")
     ap.add_argument("--cublas", action="store_true", help="gemm_* ops: time torch.matmul (cuBLAS) instead")
+    ap.add_argument("--replays", type=int, default=30, help="--op forward_cfg4: graph replays")
+    ap.add_argument("--split-k", type=int, default=0, help="--op forward_cfg4: k-slices of the residual-add GEMMs")
     args = ap.parse_args(argv)
+    if args.op == "forward_cfg4":
+        forward_cfg4(args.replays, fused_residual_gemm=not args.cublas, residual_split_k=args.split_k)
+        return
     global CUBLAS
     CUBLAS = args.cublas
     cfg = ModelConfig()
@@ -220,7 +266,7 @@ def main(argv=None):
         else:
             ms = time_op(fn, args.iters, args.warmup)
         achieved = work / (ms * 1e-3) / (1e12 if bound == "tensor" else 1e9)
-        print(json.dumps({"op": op + (" (cuBLAS)" if CUBLAS and op.startswith("gemm_") else ""), "batch": "lens" if args.lens else args.batch, "tokens": int(sum(lens)),
+        print(json.dumps({"op": op + (" (cuBLAS)" if CUBLAS and op.startswith(("gemm_", "resadd_")) else ""), "batch": "lens" if args.lens else args.batch, "tokens": int(sum(lens)),
                           "attn": [cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim],
                           "segments": len(lens),
                           "max_len": int(max(lens)), "us": round(ms * 1e3, 2), "bound": bound,

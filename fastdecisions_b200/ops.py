@@ -96,6 +96,26 @@ def residual_rmsnorm(x: torch.Tensor, residual: Optional[torch.Tensor], weight: 
     return out, (residual_out if write_residual else None)
 
 
+def rmsnorm_stream(h: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, weight_offset: float = 1.0,
+                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``bf16(h * rsqrt(mean(h^2) + eps) * (weight_offset + w))`` of the residual stream ``h`` itself
+    (float32 or bf16, last dim contiguous): the norm after a GEMM that already added into ``h``."""
+    _need_cuda(h, weight)
+    if h.dtype not in (torch.float32, BF16) or h.shape[-1] != weight.numel() or h.stride(-1) != 1:
+        raise ValueError("rmsnorm_stream: h must be float32 or bf16 with the hidden size last")
+    H = h.shape[-1]
+    h2 = h.reshape(-1, H)
+    rows = h2.shape[0]
+    if out is None:
+        out = torch.empty(h.shape, device=h.device, dtype=BF16)
+    o2 = out.reshape(-1, H)
+    with torch.cuda.device(h.device):
+        _lib.call("fdk_residual_rmsnorm", None, 0, h2.data_ptr(), h2.stride(0) if rows > 1 else H,
+                  int(h.dtype == torch.float32), weight.data_ptr(), int(weight.dtype == torch.float32), o2.data_ptr(),
+                  o2.stride(0) if rows > 1 else H, None, 0, rows, H, float(eps), float(weight_offset), _stream(h))
+    return out
+
+
 @torch.library.custom_op("fastdecisions::residual_rms", mutates_args=(), device_types="cuda")
 def residual_rms(a: torch.Tensor, b: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     """Reference signature (persistent_residual_rms.py:7-9): RMSNorm(1+w, eps 1e-6) of a + b."""
@@ -583,3 +603,37 @@ def gemm_qk_norm_rope(a: torch.Tensor, w: torch.Tensor, q_norm_w: torch.Tensor, 
                   k_norm_w.data_ptr(), positions.data_ptr(), rope.data_ptr(), rope.shape[0], rope.shape[1], float(eps),
                   q.data_ptr(), kk.data_ptr(), _stream(a))
     return proj, q, kk
+
+
+def residual_add_tickets(m: int, n: int, device) -> torch.Tensor:
+    """Zeroed slice-ticket array for ``gemm_residual_add`` of an ``m x n`` output (reusable: every
+    completed call leaves it zeroed; calls sharing it must not overlap on the GPU)."""
+    return torch.zeros(4 * ((m + 127) // 128) * ((n + 255) // 256) + 2, dtype=torch.int32, device=device)
+
+
+def gemm_residual_add(a: torch.Tensor, w: torch.Tensor, h: torch.Tensor, split_k: int = 0,
+                      tickets: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``h += a @ w^T`` in place: ``a [m, k]`` bf16, ``w [n, k]`` bf16 (nn.Linear layout), ``h [m, n]``
+    float32 (the residual stream).  The product is added from fp32 accumulators (never rounded to
+    bf16); ``split_k`` slices K (0: chosen by the library to fill the SMs), the slices adding in a
+    fixed order kept by ``tickets`` (``residual_add_tickets``; allocated here when not given).
+    Returns ``h``."""
+    _need_cuda(a, w, h)
+    if a.dim() != 2 or w.dim() != 2 or a.shape[1] != w.shape[1] or h.shape != (a.shape[0], w.shape[0]):
+        raise ValueError("gemm_residual_add: expected a [m, k], w [n, k] and h [m, n]")
+    if a.dtype != BF16 or w.dtype != BF16 or h.dtype != torch.float32:
+        raise ValueError("gemm_residual_add: a and w must be bf16 and h float32")
+    if a.stride(1) != 1 or w.stride(1) != 1 or h.stride(1) != 1:
+        raise ValueError("gemm_residual_add: unit column strides required")
+    m, k = a.shape
+    n = w.shape[0]
+    need = 4 * ((m + 127) // 128) * ((n + 255) // 256) + 2
+    if tickets is None:
+        tickets = residual_add_tickets(m, n, a.device)
+    elif tickets.dtype != torch.int32 or tickets.numel() < need:
+        raise ValueError(f"gemm_residual_add: tickets must be int32 with at least {need} elements")
+    with torch.cuda.device(a.device):
+        _lib.call("fdk_gemm_bf16_residual_add", a.data_ptr(), a.stride(0) if m > 1 else k, w.data_ptr(),
+                  w.stride(0) if n > 1 else k, h.data_ptr(), h.stride(0) if m > 1 else n, m, n, k, int(split_k),
+                  tickets.data_ptr(), _stream(a))
+    return h

@@ -53,6 +53,8 @@ const char* fdk_get_last_error_string(void);
  * is float32 and s is not rounded (s = x + residual in fp32).  x and out are bf16; weight is
  * bf16, or float32 when weight_is_fp32 != 0.  Row strides ld_* are in elements and must keep
  * every row 16-byte aligned; hidden % 8 == 0, hidden <= 8192.  residual_out may alias residual.
+ * x may be NULL when residual is given: s = residual (the norm of a residual stream whose
+ * producer already added into it, as fdk_gemm_bf16_residual_add does).
  */
 int fdk_residual_rmsnorm(const void* x, int64_t ld_x, const void* residual, int64_t ld_residual,
                          int residual_is_fp32, const void* weight, int weight_is_fp32, void* out,
@@ -271,6 +273,25 @@ int fdk_gemm_bf16_qk_norm_rope(const void* a, int64_t lda, const void* b, int64_
                                const void* k_norm_w, const int32_t* positions,
                                const float* rope_table, int64_t max_pos, int rot_dim, float eps,
                                void* q_out, void* k_out, void* stream);
+
+/*
+ * Projection GEMM that adds into the residual stream: h [m, n] (float32, row stride ldh) += A B^T,
+ * the residual adds of the decoder layer ([tf]:775 and 781) fused into the out-projection and
+ * down-projection GEMMs that produce them ([tf]:532, 691, 708).  The fp32 accumulators are added
+ * into h by TMA reduce-add stores: the layer output is never rounded to bf16, and K can be split
+ * into slices that each add their partial sum (split_k: 1-16 slices; 0 = 1: measured, ordered
+ * slices cost more than the idle SMs they fill at m = 1536, n = 2048).
+ * The slices of a tile add in a fixed order (slice 0 first), so results are reproducible; the
+ * order is kept with `tickets`: int32 [4 x ceil(m / 128) x ceil(n / 256) + 2], zero before the
+ * first call and left zero by every call that completes (re-zero it after an error of this call).
+ * With split slices the CTAs claim work dynamically, so the call stays deadlock-free when other
+ * kernels hold some of the SMs.
+ * tickets == NULL runs without splitting.  n and k multiples of 8; pointers and rows 16-byte
+ * aligned (ldh a multiple of 4).  Calls sharing one tickets array must not overlap on the GPU.
+ */
+int fdk_gemm_bf16_residual_add(const void* a, int64_t lda, const void* b, int64_t ldb, float* h,
+                               int64_t ldh, int64_t m, int64_t n, int64_t k, int split_k,
+                               int32_t* tickets, void* stream);
 
 /* Token embedding gather: out[t, :] = table[ids[t], :] ([tf]:1243).  ids int32. */
 int fdk_embed(const int32_t* ids, const void* table, int64_t vocab, int64_t hidden, void* out,

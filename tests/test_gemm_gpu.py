@@ -90,3 +90,45 @@ def test_gemm_qk_norm_rope_epilogue(m, hq, hkv, D):
     # the output gate and v columns are the plain product
     check(proj.reshape(m, -1)[:, :2 * hq * D].reshape(m, hq, 2, D)[:, :, 1], qg[:, :, 1])
     check(proj[:, (2 * hq + hkv) * D:], full[:, (2 * hq + hkv) * D:])
+
+
+@pytest.mark.parametrize("m,n,k,split", [(1536, 2048, 2048, 0), (1536, 2048, 6144, 0), (777, 2048, 2048, 1),
+                                         (300, 264, 136, 3), (5, 256, 64, 0), (4097, 512, 1024, 2)])
+def test_gemm_residual_add(m, n, k, split):
+    """h (float32) += a w^T from the fp32 accumulators, k split into slices that each add their part;
+    against the float32 product (the residual adds of [tf]:775, 781)."""
+    a, w = inputs(m, n, k, m + 3 * n + k)
+    h0 = torch.randn(m, n, generator=torch.Generator().manual_seed(m))
+    h = h0.cuda()
+    ops.gemm_residual_add(a.cuda(), w.cuda(), h, split_k=split)
+    torch.cuda.synchronize()
+    assert _lib.poll_device_error() == 0
+    ref = h0 + a.float() @ w.float().t()
+    err = (h.cpu() - ref).abs().max().item()
+    assert err <= 1e-4 * max(1.0, ref.abs().max().item()), err
+
+
+def test_rmsnorm_of_the_stream_alone():
+    g = torch.Generator().manual_seed(3)
+    h = torch.randn(100, 2048, generator=g)
+    w = (0.02 * torch.randn(2048, generator=g)).bfloat16()
+    got = ops.rmsnorm_stream(h.cuda(), w.cuda())
+    torch.testing.assert_close(got.cpu().float(), O.rmsnorm_offset(h, w), rtol=0.008, atol=0.002)
+
+
+def test_gemm_residual_add_is_reproducible_with_split_k():
+    """The k-slices add into h in a fixed order: repeated calls give bit-identical results, and the
+    ticket array is left zeroed."""
+    a, w = inputs(1536, 2048, 6144, 77)
+    a, w = a.cuda(), w.cuda()
+    h0 = torch.randn(1536, 2048, generator=torch.Generator().manual_seed(78)).cuda()
+    tk = ops.residual_add_tickets(1536, 2048, "cuda")
+    outs = []
+    for _ in range(3):
+        h = h0.clone()
+        ops.gemm_residual_add(a, w, h, split_k=4, tickets=tk)
+        outs.append(h)
+    torch.cuda.synchronize()
+    assert _lib.poll_device_error() == 0
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    assert int(tk.abs().sum()) == 0
