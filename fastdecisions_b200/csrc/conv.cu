@@ -43,6 +43,7 @@ constexpr int CONV_HALO = 3;
 constexpr int CONV_MAX_TILES_PER_CTA = 4;
 constexpr int CONV_CTAS_PER_SM = 6;
 constexpr int64_t CONV_DIRECT_MAX_TOKENS = 8192;  // up to this many tokens the direct kernel runs
+constexpr int CONV_DIRECT_RPT = 8;  // tokens per thread of the direct kernel (16 measured slower: 14.2 vs 13.0 us at config 2)
 constexpr int CONV_SROWS = CONV_ROWS + CONV_HALO;
 constexpr int CONV_RPT = 8;             // rows per thread
 
@@ -172,14 +173,14 @@ __global__ void __launch_bounds__(CONV_THREADS, 6) packed_conv_silu_smem_kernel(
 // halo included; halo rows are L2 hits) are loaded with independent 16-byte loads before any
 // arithmetic, so every thread has its whole input in flight at once.  Channel pairs use the packed
 // fp32 pipe (fma.rn.f32x2): the same roundings per lane as the scalar chain of the staged kernel.
-template <int KW>
+template <int KW, int RPT>
 __global__ void __launch_bounds__(128) packed_conv_silu_direct_kernel(
     const bf16* __restrict__ x, int64_t ldx, const bf16* __restrict__ w, int64_t ntok, int64_t period,
     const int32_t* __restrict__ cu, int nseg, int channels, int key_dim, bf16* __restrict__ q,
     bf16* __restrict__ k, bf16* __restrict__ v) {
   const int lane = threadIdx.x & 31, wg = threadIdx.x >> 5;
   const int c0 = (blockIdx.x * 32 + lane) * 8;
-  const int64_t r0 = ((int64_t)blockIdx.y * 4 + wg) * CONV_RPT;
+  const int64_t r0 = ((int64_t)blockIdx.y * 4 + wg) * RPT;
   if (c0 >= channels || r0 >= ntok) return;  // no barriers below
   int64_t seg0, nxt;
   if (cu != nullptr) {
@@ -189,9 +190,9 @@ __global__ void __launch_bounds__(128) packed_conv_silu_direct_kernel(
     seg0 = (r0 / period) * period;
     nxt = seg0 + period;
   }
-  uint4 raw[CONV_RPT + CONV_HALO];
+  uint4 raw[RPT + CONV_HALO];
 #pragma unroll
-  for (int j = 0; j < CONV_RPT + CONV_HALO; ++j) {
+  for (int j = 0; j < RPT + CONV_HALO; ++j) {
     const int64_t t = r0 - CONV_HALO + j;
     raw[j] = (t >= seg0 && t < ntok) ? ldg_stream(x + t * ldx + c0) : make_uint4(0u, 0u, 0u, 0u);
   }
@@ -222,7 +223,7 @@ __global__ void __launch_bounds__(128) packed_conv_silu_direct_kernel(
   };
   const float2 half2 = make_float2(0.5f, 0.5f);
 #pragma unroll
-  for (int i = 0; i < CONV_RPT; ++i) {
+  for (int i = 0; i < RPT; ++i) {
     const int64_t t = r0 + i;
     if (t >= ntok) break;
     if (t == nxt) {  // a segment starts inside this row group: earlier rows are not its history
@@ -293,12 +294,13 @@ extern "C" int fdk_packed_conv_silu(const void* x, int64_t ld_x, const void* wei
     if (dev >= 0 && dev < 64) carveout_set[dev] = true;
   }
   if (ntok <= CONV_DIRECT_MAX_TOKENS) {
-    const dim3 dgrid((unsigned)((channels / 8 + 31) / 32), (unsigned)((ntok + 4 * CONV_RPT - 1) / (4 * CONV_RPT)));
+    constexpr int R = CONV_DIRECT_RPT;
+    const dim3 dgrid((unsigned)((channels / 8 + 31) / 32), (unsigned)((ntok + 4 * R - 1) / (4 * R)));
     switch (kernel_width) {
-      case 4: packed_conv_silu_direct_kernel<4><<<dgrid, 128, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
-      case 3: packed_conv_silu_direct_kernel<3><<<dgrid, 128, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
-      case 2: packed_conv_silu_direct_kernel<2><<<dgrid, 128, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
-      default: packed_conv_silu_direct_kernel<1><<<dgrid, 128, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
+      case 4: packed_conv_silu_direct_kernel<4, R><<<dgrid, 128, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
+      case 3: packed_conv_silu_direct_kernel<3, R><<<dgrid, 128, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
+      case 2: packed_conv_silu_direct_kernel<2, R><<<dgrid, 128, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
+      default: packed_conv_silu_direct_kernel<1, R><<<dgrid, 128, 0, s>>>(xb, ld_x, wb, ntok, seqlen, cu_seqlens, nseg, (int)channels, (int)key_dim, qb, kb, vb); break;
     }
     return check_launch("packed_conv_silu");
   }

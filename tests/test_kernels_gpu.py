@@ -405,8 +405,9 @@ def test_gdn_fused_matches_separate_ops(lens):
     assert _lib.poll_device_error() == 0
 
 
-def test_gdn_fused_against_oracle():
-    H, lens = 2, [100, 1, 70]
+@pytest.mark.parametrize("H,lens", [(2, [100, 1, 70]), (16, [1536])])
+def test_gdn_fused_against_oracle(H, lens):
+    # (16, [1536]): one GDN layer of config 4 through the single-launch pipelined path
     proj, conv, A_log, dt, cu, C, vd = gdn_proj_inputs(lens, H, 22)
     fused = ops.gdn_fused_delta_rule(dev(proj), dev(conv), dev(A_log), dev(dt), H, C + vd + H, C + vd, dev(cu))
     q, k, v = O.packed_conv_silu(proj[:, :C].unsqueeze(0), conv, cu_seqlens=cu, key_dim=H * 128, value_dim=vd)
