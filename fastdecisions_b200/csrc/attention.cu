@@ -41,6 +41,11 @@ enum { B_Q = 0, B_KF0, B_KF1, B_KE0, B_KE1, B_VF0, B_VF1, B_VE0, B_VE1, B_SA, B_
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 8 * NBAR + 16 + 1024;  // + slack for 1024-B alignment
 constexpr int NUM_THREADS = 320;
 constexpr uint32_t TM_SA = 0, TM_SB = 128, TM_OA = 256, TM_OB = 384, TM_COLS = 512;
+// head_dim 128 runs one query head a CTA when (segments x head pairs x query tiles) is at most this.
+// Measured (16 q / 4 kv heads): one 1536 segment 41.0 -> 29.3 us, one 2048 segment 49.1 -> 37.7 us;
+// at one 4096 segment (256 pair-tiles) 82.9 vs 92.9 us and on packed config-5 batches the two-head
+// kernel is faster.
+constexpr int64_t ONE_HEAD_MAX_PAIR_TILES = 148;
 constexpr long long DRAIN_BUDGET = 2000000000LL;
 
 __device__ int g_device_error = 0;
@@ -319,32 +324,46 @@ gqa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
 }
 
 // ---------------------------------------------------------------------------------------------
-// head_dim 256 (the reference op's own shape: native_gqa_kernel.py:132-133 accepts only D = 256,
-// run with 8 query / 2 KV heads).  One CTA = 128 queries of ONE query head: S (128 x 64 fp32) and O
-// (128 x 256 fp32) of two heads would not fit 512 TMEM columns.  KV blocks are 64 keys, so the
-// shared-memory rings fit beside Q: Q [4 boxes][128 rows][128 B] 64 KB, K and V two stages of
-// [4 boxes][64 rows][128 B] (32 KB) each -- 192 KB.  TMEM: S ping-pong [0,64) and [64,128), O
-// [256,512).  Warps 0-3 softmax (thread = query row = TMEM lane), warp 4 TMA producer, warp 5 TMEM
-// allocator + MMA issuer.  The issuer keeps one S block ahead of the softmax:
+// One query head a CTA.  Used for head_dim 256 (the reference op's own shape:
+// native_gqa_kernel.py:132-133 accepts only D = 256, run with 8 query / 2 KV heads), where S and O
+// of two heads would not fit 512 TMEM columns, with 64-key KV blocks: Q 64 KB, K and V two stages of
+// 32 KB each -- 192 KB of shared memory; and for head_dim 128 when the two-head kernel's grid would
+// leave SMs idle (short segments), with 128-key blocks: 160 KB.  TMEM: S ping-pong [0, BN) and
+// [BN, 2 BN), O [256, 256 + D).  Warps 0-3 softmax (thread = query row = TMEM lane), warp 4 TMA
+// producer, warp 5 TMEM allocator + MMA issuer.  The issuer keeps one S block ahead of the softmax:
 //     S(0), S(1); then per block j: [P(j) ready] O += P(j) V(j); S(j+2) into P(j)'s buffer
 // (MMAs of one thread run in issue order, so S(j+2) overwrites P(j) only after the PV reading it),
 // so the tensor core runs PV(j) and S(j+2) while the softmax works on S(j+1).  A lazy O rescale at
 // block j waits for PV(j-1) on its own barrier: S(j)'s commit covers PV(j-2), and PV(j) needs P(j),
 // so that barrier has completed j-1 or j times.
-namespace d256 {
-constexpr int BM = 128, BN = 64, HD = 256;
-constexpr uint32_t QBOX = 128 * 128, KBOX = 64 * 128;  // one swizzle-128B box: rows x 64 bf16
-constexpr uint32_t QT = 4 * QBOX, KT = 4 * KBOX;       // a full 256-wide row block
-constexpr uint32_t OFF_Q = 0, OFF_K0 = QT, OFF_K1 = QT + KT, OFF_V0 = QT + 2 * KT, OFF_V1 = QT + 3 * KT,
-                   OFF_BAR = QT + 4 * KT;
+namespace onehead {
+// Geometry of one instantiation: head_dim HD_ (128 or 256) and BN_ keys a KV block (128 or 64).
+// Shared memory: Q [HD/64 boxes][128 rows][128 B], K and V two stages of [HD/64][BN][128 B] each.
+// TMEM: S ping-pong [0, BN) and [BN, 2 BN), O [256, 256 + HD).
+template <int HD_, int BN_>
+struct Geo {
+  static constexpr int BM = 128, BN = BN_, HD = HD_, NBX = HD_ / 64;
+  static constexpr uint32_t QBOX = 128 * 128, KBOX = (uint32_t)BN_ * 128;
+  static constexpr uint32_t QT = NBX * QBOX, KT = NBX * KBOX;
+  static constexpr uint32_t OFF_Q = 0, OFF_K0 = QT, OFF_K1 = QT + KT, OFF_V0 = QT + 2 * KT, OFF_V1 = QT + 3 * KT,
+                            OFF_BAR = QT + 4 * KT;
+};
 enum { B_Q = 0, B_KF0, B_KF1, B_KE0, B_KE1, B_VF0, B_VF1, B_VE0, B_VE1, B_S0, B_S1, B_P0, B_P1, B_PV, B_O, NBAR };
-constexpr uint32_t SMEM_BYTES = OFF_BAR + 8 * NBAR + 16 + 1024;
+template <int HD_, int BN_>
+constexpr uint32_t smem_bytes() { return Geo<HD_, BN_>::OFF_BAR + 8 * NBAR + 16 + 1024; }
 constexpr int NUM_THREADS = 192;
 constexpr uint32_t TM_S = 0, TM_O = 256, TM_COLS = 512;
 
+template <int HD_, int BN_>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-gqa_fwd_d256_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                    const __grid_constant__ CUtensorMap tv, const Params p) {
+gqa_fwd_1head_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                     const __grid_constant__ CUtensorMap tv, const Params p) {
+  using G = Geo<HD_, BN_>;
+  constexpr int BM = G::BM, BN = G::BN, HD = G::HD, NBX = G::NBX;
+  constexpr uint32_t QBOX = G::QBOX, KBOX = G::KBOX, QT = G::QT, KT = G::KT;
+  constexpr uint32_t OFF_Q = G::OFF_Q, OFF_K0 = G::OFF_K0, OFF_K1 = G::OFF_K1, OFF_V0 = G::OFF_V0,
+                     OFF_V1 = G::OFF_V1, OFF_BAR = G::OFF_BAR;
+  static_assert(2 * BN <= (int)TM_O && (int)TM_O + HD <= (int)TM_COLS, "TMEM layout");
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -387,7 +406,7 @@ gqa_fwd_d256_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
       prefetch_tmap(&tv);
       mbar_expect_tx(bar(B_Q), QT);
 #pragma unroll
-      for (int b = 0; b < 4; ++b) tma_load_2d(base + OFF_Q + b * QBOX, &tq, bar(B_Q), h * HD + 64 * b, seg0 + m0);
+      for (int b = 0; b < NBX; ++b) tma_load_2d(base + OFF_Q + b * QBOX, &tq, bar(B_Q), h * HD + 64 * b, seg0 + m0);
       int issued_k = 0, issued_v = 0;
       for (int j = 0; j < n_kv; ++j) {
         const int ks = j & 1;
@@ -395,13 +414,13 @@ gqa_fwd_d256_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
         const uint32_t kdst = base + (ks ? OFF_K1 : OFF_K0);
         mbar_expect_tx(bar(B_KF0 + ks), KT);
 #pragma unroll
-        for (int b = 0; b < 4; ++b) tma_load_2d(kdst + b * KBOX, &tk, bar(B_KF0 + ks), hk * HD + 64 * b, seg0 + j * BN);
+        for (int b = 0; b < NBX; ++b) tma_load_2d(kdst + b * KBOX, &tk, bar(B_KF0 + ks), hk * HD + 64 * b, seg0 + j * BN);
         issued_k = j + 1;
         if (j >= 2 && !mbar_wait(bar(B_VE0 + ks), ((j >> 1) - 1) & 1, abort_flag)) break;
         const uint32_t vdst = base + (ks ? OFF_V1 : OFF_V0);
         mbar_expect_tx(bar(B_VF0 + ks), KT);
 #pragma unroll
-        for (int b = 0; b < 4; ++b) tma_load_2d(vdst + b * KBOX, &tv, bar(B_VF0 + ks), hk * HD + 64 * b, seg0 + j * BN);
+        for (int b = 0; b < NBX; ++b) tma_load_2d(vdst + b * KBOX, &tv, bar(B_VF0 + ks), hk * HD + 64 * b, seg0 + j * BN);
         issued_v = j + 1;
       }
       // drain: every issued load must have landed before shared memory is released
@@ -415,25 +434,25 @@ gqa_fwd_d256_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
       constexpr uint32_t ID_QK = idesc_bf16(128, BN, false, false);
       constexpr uint32_t ID_PV = idesc_bf16(128, HD, false, true);  // V is MN-major (d contiguous)
       const uint64_t dq = sdesc_sw128(base + OFF_Q, 16, 1024);
-      // S(j) = Q K_j^T into S buffer j & 1: K = 256 in 16 steps of 16 (4 per swizzle box)
+      // S(j) = Q K_j^T into S buffer j & 1: K = D in D / 16 steps of 16 (4 per swizzle box)
       auto issue_s = [&](int j) {
         const uint64_t dk = sdesc_sw128(base + ((j & 1) ? OFF_K1 : OFF_K0), 16, 1024);
 #pragma unroll
-        for (int kk = 0; kk < 16; ++kk) {
+        for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t qoff = ((kk >> 2) * QBOX + (kk & 3) * 32) >> 4;
           const uint32_t koff = ((kk >> 2) * KBOX + (kk & 3) * 32) >> 4;
-          umma_ss(tmem + TM_S + 64u * (uint32_t)(j & 1), dq + qoff, dk + koff, ID_QK, kk > 0);
+          umma_ss(tmem + TM_S + (uint32_t)BN * (uint32_t)(j & 1), dq + qoff, dk + koff, ID_QK, kk > 0);
         }
         umma_commit(bar(B_S0 + (j & 1)));
         umma_commit(bar(B_KE0 + (j & 1)));
       };
-      // O += P(j) V(j): P as bf16 pairs in the first 32 columns of S buffer j & 1; V's four 64-wide
-      // d groups are KBOX apart (lbo), its 8-key atoms 1024 B apart (sbo); K = 64 keys in 4 steps
+      // O += P(j) V(j): P as bf16 pairs in the first BN / 2 columns of S buffer j & 1; V's 64-wide d
+      // groups are KBOX apart (lbo), its 8-key atoms 1024 B apart (sbo); K = BN keys in steps of 16
       auto issue_pv = [&](int j) {
         const uint64_t dv = sdesc_sw128(base + ((j & 1) ? OFF_V1 : OFF_V0), KBOX, 1024);
-        const uint32_t tp = tmem + TM_S + 64u * (uint32_t)(j & 1);
+        const uint32_t tp = tmem + TM_S + (uint32_t)BN * (uint32_t)(j & 1);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
+        for (int kk = 0; kk < BN / 16; ++kk)
           umma_ts(tmem + TM_O, tp + 8 * kk, dv + (uint32_t)(kk * 2048 >> 4), ID_PV, (j > 0 || kk > 0) ? 1u : 0u);
         umma_commit(bar(B_PV));
         umma_commit(bar(B_VE0 + (j & 1)));
@@ -474,20 +493,20 @@ gqa_fwd_d256_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      const uint32_t tS = tmem + lane_base + TM_S + 64u * (uint32_t)(j & 1);
+      const uint32_t tS = tmem + lane_base + TM_S + (uint32_t)BN * (uint32_t)(j & 1);
       if (!__all_sync(0xffffffffu, mbar_wait(bar(B_S0 + (j & 1)), (j >> 1) & 1, abort_flag) ? 1 : 0)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t sr[2][32];
-      tmem_ld32(tS, sr[0]);
-      tmem_ld32(tS + 32, sr[1]);
+      uint32_t sr[BN / 32][32];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS + c * 32, sr[c]);
       tmem_ld_wait();
       const int lim = qpos - j * BN;  // key column c is visible when c <= lim
       if (lim < BN - 1) {             // a block that crosses the diagonal: causal mask
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
+        for (int c = 0; c < BN / 32; ++c)
 #pragma unroll
           for (int i = 0; i < 32; ++i)
             if (c * 32 + i > lim) sr[c][i] = __float_as_uint(-INFINITY);
@@ -496,7 +515,7 @@ gqa_fwd_d256_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
 #pragma unroll
       for (int a = 0; a < 8; ++a) mx8[a] = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 2; ++c)
+      for (int c = 0; c < BN / 32; ++c)
 #pragma unroll
         for (int i = 0; i < 32; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sr[c][i]));
       const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
@@ -514,16 +533,17 @@ gqa_fwd_d256_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
       float sum8[8];
 #pragma unroll
       for (int a = 0; a < 8; ++a) sum8[a] = 0.f;
-      uint32_t pk[32];
+      uint32_t pk[BN / 64][32];
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
+      for (int c = 0; c < BN / 2; ++c) {
         const float e0 = ex2(fmaf(__uint_as_float(sr[(2 * c) >> 5][(2 * c) & 31]), sl2, -m_run));
         const float e1 = ex2(fmaf(__uint_as_float(sr[(2 * c + 1) >> 5][(2 * c + 1) & 31]), sl2, -m_run));
         sum8[(2 * c) & 7] += e0;
         sum8[(2 * c + 1) & 7] += e1;
-        pk[c] = pack_bf16x2(e0, e1);
+        pk[c >> 5][c & 31] = pack_bf16x2(e0, e1);
       }
-      tmem_st32(tS, pk);
+#pragma unroll
+      for (int c = 0; c < BN / 64; ++c) tmem_st32(tS + c * 32, pk[c]);
       const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
       l_run = l_run * alpha + sum;
       // O row *= alpha once PV(j-1) has completed (warp-uniform: the TMEM accesses are collective)
@@ -534,7 +554,7 @@ gqa_fwd_d256_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
         }
         tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c < 8; ++c) {
+        for (int c = 0; c < HD / 32; ++c) {
           uint32_t o[32];
           tmem_ld32(tO + c * 32, o);
           tmem_ld_wait();
@@ -556,7 +576,7 @@ gqa_fwd_d256_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
       bf16* orow = p.out + (tok * p.hq + h) * HD;
       const bf16* grow = p.gate ? p.gate + tok * p.ld_gate + (int64_t)h * p.gate_hstride : nullptr;
 #pragma unroll 1
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 0; c < HD / 32; ++c) {
         uint32_t o[32];
         tmem_ld32(tO + c * 32, o);
         tmem_ld_wait();
@@ -588,7 +608,7 @@ gqa_fwd_d256_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
   }
   if (tid == 0 && *abort_flag) atomicExch(&g_device_error, 1);
 }
-}  // namespace d256
+}  // namespace onehead
 
 using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
 
@@ -646,7 +666,11 @@ extern "C" int fdk_gqa_fwd(const void* q, int64_t ld_q, const void* k, int64_t l
       (gate && (!aligned16(gate) || ld_gate % 8)))
     return set_error(FDK_ERR_ALIGNMENT, "gqa_fwd: pointers and strides must be 16-byte aligned");
   if (tokens == 0 || max_seqlen == 0) return FDK_OK;
-  const int kv_rows = HD == 256 ? d256::BN : BN;
+  // head_dim 128: two query heads a CTA, unless that grid would leave SMs idle (short segments, e.g.
+  // one 1536-token request: 96 CTAs for 148 SMs) -- then one head a CTA, twice the CTAs
+  const int64_t mtiles = (max_seqlen + BM - 1) / BM;
+  const bool one_head = HD == 256 || num_segments * (hq / 2) * mtiles <= (int64_t)ONE_HEAD_MAX_PAIR_TILES;
+  const int kv_rows = HD == 256 ? 64 : 128;
   CUtensorMap mq, mk, mv;
   if (int st = make_map(&mq, q, hq * HD, tokens, ld_q)) return st;
   if (int st = make_map(&mk, k, hkv * HD, tokens, ld_k, kv_rows)) return st;
@@ -661,14 +685,21 @@ extern "C" int fdk_gqa_fwd(const void* q, int64_t ld_q, const void* k, int64_t l
   prm.gate = static_cast<const bf16*>(gate);
   prm.ld_gate = ld_gate;
   prm.gate_hstride = (int)(gate_interleaved ? 2 * HD : HD);
-  const int64_t mtiles = (max_seqlen + BM - 1) / BM;
-  if (HD == 256) {
-    if (int st = ensure_smem_attr((const void*)d256::gqa_fwd_d256_kernel, (int)d256::SMEM_BYTES, "gqa_fwd")) return st;
+  if (one_head) {
     if (mtiles > 65535 || num_segments * hq > 0x7fffffff)
       return set_error(FDK_ERR_UNSUPPORTED, "gqa_fwd: too many query tiles or segments");
     dim3 grid((unsigned)(num_segments * hq), (unsigned)mtiles);
-    d256::gqa_fwd_d256_kernel<<<grid, d256::NUM_THREADS, d256::SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(mq, mk, mv, prm);
-    return check_launch("gqa_fwd (head_dim 256)");
+    cudaStream_t st_ = static_cast<cudaStream_t>(stream);
+    if (HD == 256) {
+      constexpr uint32_t sm = onehead::smem_bytes<256, 64>();
+      if (int st = ensure_smem_attr((const void*)onehead::gqa_fwd_1head_kernel<256, 64>, (int)sm, "gqa_fwd")) return st;
+      onehead::gqa_fwd_1head_kernel<256, 64><<<grid, onehead::NUM_THREADS, sm, st_>>>(mq, mk, mv, prm);
+    } else {
+      constexpr uint32_t sm = onehead::smem_bytes<128, 128>();
+      if (int st = ensure_smem_attr((const void*)onehead::gqa_fwd_1head_kernel<128, 128>, (int)sm, "gqa_fwd")) return st;
+      onehead::gqa_fwd_1head_kernel<128, 128><<<grid, onehead::NUM_THREADS, sm, st_>>>(mq, mk, mv, prm);
+    }
+    return check_launch("gqa_fwd (one head a CTA)");
   }
   if (int st = ensure_smem_attr((const void*)gqa_fwd_kernel, (int)SMEM_BYTES, "gqa_fwd")) return st;
   if (mtiles > 65535 || num_segments * (hq / 2) > 0x7fffffff)

@@ -43,6 +43,15 @@ def test_small_segments(lens):
     check(o, O.gqa_attention_varlen(q, k, v, cu))
 
 
+def test_many_short_segments_two_head_path():
+    # 40 segments x 8 head pairs x 3 query tiles fill the SMs: the two-heads-a-CTA kernel (the small
+    # cases above run one head a CTA)
+    lens = [300, 257, 129, 384] * 10
+    q, k, v = make(sum(lens), 16, 4, seed=41)
+    o, cu = run(q, k, v, lens)
+    check(o, O.gqa_attention_varlen(q, k, v, cu))
+
+
 def test_config3_varlen():
     # 4 requests, lengths uniform in [256, 4096] from seed 17
     g = torch.Generator().manual_seed(17)
