@@ -330,6 +330,7 @@ __device__ __forceinline__ bool prep_sync_and(bool v) {
 // every barrier (each completes once per tile).  Returns false if a bounded wait ran out.
 template <bool CONV, bool PIPE>
 __device__ __forceinline__ bool prep_tile(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                                          const CUtensorMap& mw_st, const CUtensorMap& mut_st,
                                           const PrepIn& in, const int4* __restrict__ info, int heads, float scale,
                                           uint8_t* __restrict__ tiles, int ci, int h, uint32_t base, uint8_t* sb,
                                           uint32_t tmem, uint32_t par) {
@@ -431,7 +432,8 @@ __device__ __forceinline__ bool prep_tile(const CUtensorMap& mq, const CUtensorM
   if (ok) {
     // 2. l2-normalise k and q rows (q also times scale) in place, zero rows past the length;
     //    decayed copies Kg = k e^(G_last - G), Qg = q e^G out (from the bf16-rounded normalised
-    //    values the products see).  Four threads per row, 32 features each.
+    //    values the products see).  Four threads per row; thread `part` takes the 16-byte chunks
+    //    part, part + 4, part + 8, part + 12, so each warp store writes 64 contiguous bytes a row.
     const int row = tid >> 2, part = tid & 3;
     const bool valid = row < len;
 #pragma unroll
@@ -439,7 +441,7 @@ __device__ __forceinline__ bool prep_tile(const CUtensorMap& mq, const CUtensorM
       const int srow = rr * 64 + row;
       uint4 u[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) u[j] = *reinterpret_cast<const uint4*>(sb + A1 + sw128_off(srow, part * 4 + j, 128));
+      for (int j = 0; j < 4; ++j) u[j] = *reinterpret_cast<const uint4*>(sb + A1 + sw128_off(srow, part + 4 * j, 128));
       // packed fp32 pipe (f32x2) for the sum of squares and both scalings
       float2 ss2 = make_float2(0.f, 0.f);
 #pragma unroll
@@ -457,7 +459,7 @@ __device__ __forceinline__ bool prep_tile(const CUtensorMap& mq, const CUtensorM
       const float inv = valid ? rsqrtf(ss + 1e-6f) * (rr ? scale : 1.0f) : 0.f;
       const float dec = rr ? exp2f(G2[row]) : exp2f(G2[63] - G2[row]);
       const float2 inv2 = make_float2(inv, inv), dec2 = make_float2(dec, dec);
-      uint4* gout = reinterpret_cast<uint4*>(tile + (rr ? OFF_QG : OFF_KG) + (size_t)row * 256 + part * 64);
+      uint4* gout = reinterpret_cast<uint4*>(tile + (rr ? OFF_QG : OFF_KG) + (size_t)row * 256);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const __nv_bfloat162* hp = reinterpret_cast<const __nv_bfloat162*>(&u[j]);
@@ -471,8 +473,8 @@ __device__ __forceinline__ bool prep_tile(const CUtensorMap& mq, const CUtensorM
           const float2 d = __fmul2_rn(__bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&np[e])), dec2);
           dp[e] = pack_bf16x2(d.x, d.y);
         }
-        *reinterpret_cast<uint4*>(sb + A1 + sw128_off(srow, part * 4 + j, 128)) = nb;
-        gout[j] = db;
+        *reinterpret_cast<uint4*>(sb + A1 + sw128_off(srow, part + 4 * j, 128)) = nb;
+        gout[part + 4 * j] = db;
       }
     }
     fence_proxy_async_smem();
@@ -690,14 +692,25 @@ __device__ __forceinline__ bool prep_tile(const CUtensorMap& mq, const CUtensorM
     tmem_ld32(ta, v[0]);
     tmem_ld32(ta + 32, v[1]);
     tmem_ld_wait();
-    uint4* dst = reinterpret_cast<uint4*>(tile + (which ? OFF_W : OFF_UT) + (size_t)r * 128);
+    // staged 128-byte-swizzled in A1 (free: the second MMA has completed) and written as one
+    // [128][64] TMA box a tile (16-byte row pieces from 32 rows at once would be half sectors)
+    uint8_t* dst = sb + A1 + which * 16384 + r * 128;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       float f[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[j >> 2][(j & 3) * 8 + e]);
-      dst[j] = pack8(f);
+      *reinterpret_cast<uint4*>(dst + ((j ^ (r & 7)) << 4)) = pack8(f);
     }
+    fence_proxy_async_smem();
+  }
+  ok = prep_sync_and<PIPE>(ok);
+  if (ok && tid == 0) {
+    const int z = ci * heads + h;
+    tma_store_3d(&mut_st, base + A1, 0, 0, z);
+    tma_store_3d(&mw_st, base + A1 + 16384, 0, 0, z);
+    bulk_commit();
+    bulk_wait<0>();  // complete (not just read) before the tile is published or A1 is reused
   }
   // teardown: on a bounded-wait failure, let in-flight copies and MMAs land before TMEM and
   // shared memory are released
@@ -717,7 +730,8 @@ __device__ __forceinline__ bool prep_tile(const CUtensorMap& mq, const CUtensorM
 template <bool CONV>
 __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
     const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
-    const __grid_constant__ CUtensorMap mv, const PrepIn in, const int4* __restrict__ info,
+    const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mw_st,
+    const __grid_constant__ CUtensorMap mut_st, const PrepIn in, const int4* __restrict__ info,
     const int32_t* __restrict__ table, int nseg, int heads, float scale, uint8_t* __restrict__ tiles) {
   extern __shared__ uint8_t smem_raw[];
   const int ci = blockIdx.x, h = blockIdx.y;
@@ -742,7 +756,7 @@ __global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  prep_tile<CONV, false>(mq, mk, mv, in, info, heads, scale, tiles, ci, h, base, sb, tmem, 0);
+  prep_tile<CONV, false>(mq, mk, mv, mw_st, mut_st, in, info, heads, scale, tiles, ci, h, base, sb, tmem, 0);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -1263,6 +1277,7 @@ gdn_pipe_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
                 const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mw,
                 const __grid_constant__ CUtensorMap mqg, const __grid_constant__ CUtensorMap mkg,
                 const __grid_constant__ CUtensorMap ma, const __grid_constant__ CUtensorMap mut,
+                const __grid_constant__ CUtensorMap mw_st, const __grid_constant__ CUtensorMap mut_st,
                 const dprep::PrepIn in, const int4* __restrict__ info, const int32_t* __restrict__ table, int nseg,
                 int heads, float scale, uint8_t* __restrict__ tiles, const drtc::RParams rp, int rec_ctas,
                 int32_t* __restrict__ ready, int32_t* __restrict__ prep_counter, int n_tiles) {
@@ -1302,7 +1317,8 @@ gdn_pipe_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
       const int t = *claim;  // every thread reads it before the barrier that ends this iteration
       const int ci = t / heads, h = t - (t / heads) * heads;
       if (t >= n_tiles || ci >= nchunks) break;  // uniform
-      bool ok = prep_tile<CONV, true>(mq, mk, mv, in, info, heads, scale, tiles, ci, h, base, sb, tmem, local & 1);
+      bool ok = prep_tile<CONV, true>(mq, mk, mv, mw_st, mut_st, in, info, heads, scale, tiles, ci, h, base, sb, tmem,
+                                      local & 1);
       // the tile's global stores before the flag that publishes them to TMA readers; this tile's
       // shared-memory writes and TMEM loads before the next tile's TMA writes and MMAs
       asm volatile("fence.proxy.async.global;\n" ::: "memory");
@@ -1409,6 +1425,8 @@ static int run_pipelined(bool conv, const void* q, const void* k, int64_t ld_qk,
   if (int st = drtc::tile_map(&mkg, tiles, OFF_KG, DR_D, DR_C, n_tiles)) return st;
   if (int st = drtc::tile_map(&ma, tiles, OFF_A, DR_C, DR_C, n_tiles)) return st;
   if (int st = drtc::tile_map(&mut, tiles, OFF_UT, DR_C, DR_D, n_tiles, DR_D / 2)) return st;
+  CUtensorMap mut_st;  // the prep writes whole U^T tiles (the recurrence halves read 64 rows)
+  if (int st = drtc::tile_map(&mut_st, tiles, OFF_UT, DR_C, DR_D, n_tiles)) return st;
   drtc::RParams rp{cu, table, table + nseg + 1, nseg, (int)heads, tiles, init, out, fin, ready};
   const void* fn = conv ? (const void*)dpipe::gdn_pipe_kernel<true> : (const void*)dpipe::gdn_pipe_kernel<false>;
   if (int st = ensure_smem_attr(fn, (int)drtc::SMEM_BYTES, "chunk_gated_delta_rule/pipelined")) return st;
@@ -1416,11 +1434,13 @@ static int run_pipelined(bool conv, const void* q, const void* k, int64_t ld_qk,
   const unsigned grid = (unsigned)sm_count();
   if (conv)
     dpipe::gdn_pipe_kernel<true><<<grid, drtc::THREADS, drtc::SMEM_BYTES, s>>>(
-        mq, mk, mv, mw, mqg, mkg, ma, mut, in, info, table, nseg, (int)heads, scale, tiles, rp, rec_ctas, ready,
+        mq, mk, mv, mw, mqg, mkg, ma, mut, mw, mut_st, in, info, table, nseg, (int)heads, scale, tiles, rp, rec_ctas,
+        ready,
         table + nseg + 2, (int)n_tiles);
   else
     dpipe::gdn_pipe_kernel<false><<<grid, drtc::THREADS, drtc::SMEM_BYTES, s>>>(
-        mq, mk, mv, mw, mqg, mkg, ma, mut, in, info, table, nseg, (int)heads, scale, tiles, rp, rec_ctas, ready,
+        mq, mk, mv, mw, mqg, mkg, ma, mut, mw, mut_st, in, info, table, nseg, (int)heads, scale, tiles, rp, rec_ctas,
+        ready,
         table + nseg + 2, (int)n_tiles);
   return check_launch("chunk_gated_delta_rule/pipelined");
 }
@@ -1466,12 +1486,15 @@ static int run_delta_rule(bool conv, const void* q, const void* k, int64_t ld_qk
     if (int st = ensure_smem_attr(conv ? (const void*)dprep::delta_prep_kernel<true> : (const void*)dprep::delta_prep_kernel<false>,
                                   (int)dprep::SMEM_BYTES, "chunk_gated_delta_rule/prep"))
       return st;
+    CUtensorMap mw_st, mut_st;  // the prep writes its U^T / W^T tiles through these
+    if (int st = drtc::tile_map(&mw_st, tiles, OFF_W, DR_C, DR_D, lay.max_chunks * heads)) return st;
+    if (int st = drtc::tile_map(&mut_st, tiles, OFF_UT, DR_C, DR_D, lay.max_chunks * heads)) return st;
     const dim3 grid((unsigned)lay.max_chunks, (unsigned)heads);
     if (conv)
-      dprep::delta_prep_kernel<true><<<grid, dprep::THREADS, dprep::SMEM_BYTES, s>>>(mq, mk, mv, in, info, table, nseg,
+      dprep::delta_prep_kernel<true><<<grid, dprep::THREADS, dprep::SMEM_BYTES, s>>>(mq, mk, mv, mw_st, mut_st, in, info, table, nseg,
                                                                                    (int)heads, scale, tiles);
     else
-      dprep::delta_prep_kernel<false><<<grid, dprep::THREADS, dprep::SMEM_BYTES, s>>>(mq, mk, mv, in, info, table, nseg,
+      dprep::delta_prep_kernel<false><<<grid, dprep::THREADS, dprep::SMEM_BYTES, s>>>(mq, mk, mv, mw_st, mut_st, in, info, table, nseg,
                                                                                     (int)heads, scale, tiles);
     if (int st = check_launch("chunk_gated_delta_rule/prep")) return st;
   }
