@@ -65,5 +65,33 @@ def build(verbose_ptxas: bool = False, jobs: int | None = None) -> str:
     return LIB
 
 
+PHASES_LIB = os.path.join(PKG, "libfdk_phases.so")
+
+
+def build_phase_stamps() -> str:
+    """A profiling copy of the library, libfdk_phases.so: the delta-rule prep compiled with
+    FDK_PHASE_STAMPS (per-phase SM-cycle counters, read with fdk_phase_stamps_read); every other
+    object is the normal build's."""
+    build()
+    obj = os.path.join(BUILD, "delta_rule_phases.o")
+    _compile_with(os.path.join(CSRC, "delta_rule.cu"), obj, ["-DFDK_PHASE_STAMPS"])
+    objs = [o for o in sorted(glob.glob(os.path.join(BUILD, "*.o"))) if os.path.basename(o) not in
+            ("delta_rule.o", "delta_rule_phases.o")] + [obj]
+    r = subprocess.run([nvcc(), "-shared", "-o", PHASES_LIB] + objs + ARCH + ["-Xcompiler", "-fPIC", "-lcudart"],
+                       capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    return PHASES_LIB
+
+
+def _compile_with(src: str, obj: str, extra) -> None:
+    r = subprocess.run([nvcc(), "-c", src, "-o", obj] + _flags(extra), capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nvcc failed for {os.path.basename(src)}:\n{r.stdout}\n{r.stderr}")
+
+
 if __name__ == "__main__":
-    print(build(verbose_ptxas="-v" in sys.argv))
+    if "--phase-stamps" in sys.argv:
+        print(build_phase_stamps())
+    else:
+        print(build(verbose_ptxas="-v" in sys.argv))

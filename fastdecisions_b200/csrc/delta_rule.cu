@@ -24,6 +24,33 @@
 #include "common.cuh"
 #include "sm100.cuh"
 
+// Phase stamps of the prep (a profiling build only: `python -m fastdecisions_b200.build
+// --phase-stamps` compiles this file with FDK_PHASE_STAMPS into a separate libfdk_phases.so).
+// Thread 0 of every prep tile adds the SM cycles of each phase to g_phase[k]; g_phase[15] counts
+// tiles; fdk_phase_stamps_read copies and clears them.
+#ifdef FDK_PHASE_STAMPS
+__device__ unsigned long long g_phase[16];
+#define PHASE_START()                                   \
+  unsigned long long t_phase = clock64();               \
+  if (threadIdx.x == 0) atomicAdd(&g_phase[15], 1ull)
+#define PHASE(k)                                                   \
+  do {                                                             \
+    if (threadIdx.x == 0) {                                        \
+      const unsigned long long t_ = clock64();                     \
+      atomicAdd(&g_phase[k], t_ - t_phase);                        \
+      t_phase = t_;                                                \
+    }                                                              \
+  } while (0)
+extern "C" int fdk_phase_stamps_read(unsigned long long* out) {
+  if (cudaMemcpyFromSymbol(out, g_phase, sizeof(g_phase)) != cudaSuccess) return 1;
+  unsigned long long z[16] = {};
+  return cudaMemcpyToSymbol(g_phase, z, sizeof(z)) == cudaSuccess ? 0 : 1;
+}
+#else
+#define PHASE_START() do {} while (0)
+#define PHASE(k) do {} while (0)
+#endif
+
 namespace fdk {
 
 constexpr int DR_C = 64;    // chunk length
@@ -346,6 +373,7 @@ __device__ __forceinline__ bool prep_tile(const CUtensorMap& mq, const CUtensorM
   const int4 inf = info[ci];
   const int t0 = inf.x, len = inf.y, seg_start = inf.z;
   uint8_t* tile = tiles + ((size_t)ci * heads + h) * CH_BYTES;
+  PHASE_START();
   bool issued_v = false, issued_mma = false;
 
   // 1. raw k rows -> A1 rows 0-63, raw q rows -> rows 64-127 (TMA, 128-byte swizzle; rows past
@@ -421,6 +449,7 @@ __device__ __forceinline__ bool prep_tile(const CUtensorMap& mq, const CUtensorM
     conv_rows<8>(box, rs * 8, c16 & 7, first_valid, wcol, sb + A1, (isk ? 0 : 64) + rs * 8, c16);
     fence_proxy_async_smem();  // the raw boxes are refilled by TMA (V) below
   }
+  PHASE(1);
   ok = prep_sync_and<PIPE>(ok);  // also publishes G2 / beta / fw
   if (CONV && ok && tid == 0) {  // raw v columns -> the T area, landing while k / q are normalised
     mbar_expect_tx(bar0 + 8 * B_V, 2 * RAW_BOX);
@@ -481,6 +510,7 @@ __device__ __forceinline__ bool prep_tile(const CUtensorMap& mq, const CUtensorM
   }
   prep_sync<PIPE>();
 
+  PHASE(2);
   // 3. D1 = [K^; Q^] K^T  (M128 N64 K128; B is A's first 64 rows)
   if (ok && tid == 0) {
     tc_fence_after();
@@ -496,6 +526,7 @@ __device__ __forceinline__ bool prep_tile(const CUtensorMap& mq, const CUtensorM
   if (ok) ok = warp_wait(bar0 + 8 * B_MMA1, par, abort_flag);
   if (ok) tc_fence_after();
   // V rows -> A1 rows 64-127 (q^ is no longer read), landing while the solve runs
+  PHASE(3);
   if (CONV && ok) ok = warp_wait(bar0 + 8 * B_V, par, abort_flag);
   if (CONV && ok) {  // v by conv into A1 rows 64-127: thread = 8 channels x 4 tokens
     const int g8 = tid & 15, rs = tid >> 4;
@@ -511,6 +542,7 @@ __device__ __forceinline__ bool prep_tile(const CUtensorMap& mq, const CUtensorM
     issued_v = true;
   }
 
+  PHASE(4);
   // 4. rows of D1: L = -beta_i (KK^T)_ij e^(G_i - G_j) (j < i) -> smem; Aqk = (QK^T)_ij e^(G_i - G_j)
   //    (j <= i) -> workspace.  Warp w reads TMEM lane quarter w % 4, column half w / 4.
   if (ok) {
@@ -573,6 +605,7 @@ __device__ __forceinline__ bool prep_tile(const CUtensorMap& mq, const CUtensorM
   tc_fence_before();
   prep_sync<PIPE>();
 
+  PHASE(5);
   // 5. T = (I - L)^-1 in fp32.
   //    Level 0 (warps 0-1, thread = one column k of one diagonal block b): forward substitution
   //    down the column, x_r = d_rk + sum_{j<r} N_rj x_j with the FMAs in increasing j (the
@@ -608,6 +641,7 @@ __device__ __forceinline__ bool prep_tile(const CUtensorMap& mq, const CUtensorM
   }
   prep_sync<PIPE>();
   auto blk = [&](float* base_, int bi, int bj) { return base_ + (16 * bi) * LDF + 16 * bj; };
+  PHASE(6);
   // level 1: warp 0 -> T_10, warp 1 -> T_32
   if (ok && warp < 2) {
     const int j = 2 * warp, i = j + 1;
@@ -622,6 +656,7 @@ __device__ __forceinline__ bool prep_tile(const CUtensorMap& mq, const CUtensorM
     bmm16_store(acc, blk(Tf, i, j), LDF);
   }
   prep_sync<PIPE>();
+  PHASE(7);
   // level 2: X_ij (i in {2,3}, j in {0,1}) = L_i0 T_0j + L_i1 T_1j (T_01 = 0) into L's block (j, i)
   if (ok && warp < 4) {
     const int i = 2 + (warp >> 1), j = warp & 1;
@@ -632,6 +667,7 @@ __device__ __forceinline__ bool prep_tile(const CUtensorMap& mq, const CUtensorM
     bmm16_store(acc, blk(Lf, j, i), LDF);
   }
   prep_sync<PIPE>();
+  PHASE(8);
   // level 3: T_ij = T_i2 X_2j + T_i3 X_3j (T_23 = 0)
   if (ok && warp < 4) {
     const int i = 2 + (warp >> 1), j = warp & 1;
@@ -643,6 +679,7 @@ __device__ __forceinline__ bool prep_tile(const CUtensorMap& mq, const CUtensorM
   }
   prep_sync<PIPE>();
 
+  PHASE(9);
   // 6. TU = bf16(T diag(beta)), TW = bf16(T diag(beta e^G)) as K-major swizzled B tiles (over L)
   if (ok) {
     for (int e = tid; e < 64 * 8; e += THREADS) {
@@ -666,6 +703,7 @@ __device__ __forceinline__ bool prep_tile(const CUtensorMap& mq, const CUtensorM
   tc_fence_before();
   prep_sync<PIPE>();
 
+  PHASE(10);
   // 7. U^T = V^T TU^T and W^T = K^T TW^T  (M128 N64 K64; A = V / K^ MN-major, B = TU / TW K-major)
   if (ok && tid == 0) {
     if (CONV || mbar_wait(bar0 + 8 * B_V, par, abort_flag)) {
@@ -682,6 +720,7 @@ __device__ __forceinline__ bool prep_tile(const CUtensorMap& mq, const CUtensorM
     }
   }
   if (ok) ok = warp_wait(bar0 + 8 * B_MMA2, par, abort_flag);
+  PHASE(11);
   // 8. U^T rows (warps 0-3) and W^T rows (warps 4-7) -> workspace, one 128-byte row per thread
   if (ok) {
     tc_fence_after();
@@ -712,6 +751,7 @@ __device__ __forceinline__ bool prep_tile(const CUtensorMap& mq, const CUtensorM
     bulk_commit();
     bulk_wait<0>();  // complete (not just read) before the tile is published or A1 is reused
   }
+  PHASE(12);
   // teardown: on a bounded-wait failure, let in-flight copies and MMAs land before TMEM and
   // shared memory are released
   if (tid == 0 && *abort_flag) {
