@@ -201,7 +201,7 @@ def delta_rule_flops(batch, cfg) -> float:
     return cfg.linear_num_value_heads * float(np.ceil(L / 64).sum()) * 11.7e6
 
 
-def op_work(cfg, batches, fused_swiglu=True, fused_qkv=True, fused_residual=True) -> dict:
+def op_work(cfg, batches, fused_swiglu=True, fused_qkv=True, fused_residual=True, split_residual=True) -> dict:
     """Algorithmic work of one step per op type: ("tensor", FLOPs) or ("hbm", bytes).  Bytes count
     each input read once and each output written once (bf16 activations, fp32 residual stream)."""
     n_att = sum(1 for t in cfg.layer_types if t == "full_attention")
@@ -221,10 +221,14 @@ def op_work(cfg, batches, fused_swiglu=True, fused_qkv=True, fused_residual=True
     # out-projections and MLP down-projections adding into the fp32 residual stream
     from fastdecisions_b200.engine import FUSED_RESIDUAL_MIN_TOKENS
     T_res = float(sum(b.tokens for b in batches if b.tokens >= FUSED_RESIDUAL_MIN_TOKENS)) if fused_residual else 0.0
-    resadd = (n_lin * 2.0 * vd * H + n_att * 2.0 * hq * D * H + cfg.num_hidden_layers * 2.0 * I * H) * T_res
+    per_token_out_down = n_lin * 2.0 * vd * H + n_att * 2.0 * hq * D * H + cfg.num_hidden_layers * 2.0 * I * H
+    resadd = per_token_out_down * T_res
+    # smaller batches: the same projections as k-split GEMMs writing partial planes
+    partials = per_token_out_down * (T - T_res) if split_residual else 0.0
     # a layer norm moves h read (+ x read, h write) and out: 6 bytes an element after a residual-add GEMM
     w = {
-        "gemm": ("tensor", 2.0 * cfg.linear_params() * T - gate_up - qkv - resadd),  # cuBLAS projections
+        "gemm": ("tensor", 2.0 * cfg.linear_params() * T - gate_up - qkv - resadd - partials),  # cuBLAS
+        "gemm_partials": ("tensor", partials),                               # own k-split GEMM, fp32 planes
         "gemm_residual_add": ("tensor", resadd),                             # own GEMM adding into the stream
         "gemm_swiglu": ("tensor", gate_up),                                  # own tcgen05 GEMM + SwiGLU epilogue
         "gemm_qk_norm_rope": ("tensor", qkv),                                # own tcgen05 GEMM + q/k norm, RoPE
@@ -433,7 +437,7 @@ def run_ours(args, world, rank, local):
     threads = max(1, (os.cpu_count() or 1) // max(1, world))
     weights = W.synthetic_weights(cfg, threads=threads)
     engine = DecisionEngine(cfg, weights, dev, fused_swiglu_gemm=not args.cublas_mlp, fused_qkv_gemm=args.fused_qkv,
-                            fused_residual_gemm=not args.cublas_residual)
+                            fused_residual_gemm=not args.cublas_residual, split_residual_gemm=args.split_residual)
     timer = KernelTimer()
     engine.kernel_timer = timer
 
@@ -513,7 +517,7 @@ def run_ours(args, world, rank, local):
     tot = timer.totals()
     pk, pk_kind = peaks()
     work = op_work(cfg, batches, engine.fused_swiglu_gemm, engine.fused_qkv_gemm,
-                   engine.fused_residual_gemm)  # per step: {op: (bound, units)}
+                   engine.fused_residual_gemm, engine.split_residual_gemm)  # per step: {op: (bound, units)}
     roof = {}
     for name, (bound, units) in work.items():
         if name not in tot or tot[name]["total_ms"] <= 0:
@@ -676,6 +680,9 @@ def main():
     ap.add_argument("--streams", type=int, default=2, help="CUDA streams the packed batches are spread over")
     ap.add_argument("--cublas-residual", action="store_true",
                     help="out / down projections on cuBLAS with the separate residual add + RMSNorm kernel")
+    ap.add_argument("--split-residual", action="store_true",
+                    help="batches < 4096 tokens: out / down projections as k-split GEMMs into fp32 partial planes "
+                         "(default: cuBLAS, measured faster)")
     ap.add_argument("--fused-qkv", action="store_true",
                     help="attention projection as the tcgen05 GEMM with q/k norm + RoPE fused (default: cuBLAS + "
                          "the separate kernel, measured faster)")

@@ -44,6 +44,8 @@ SIGNATURES = {
     "fdk_embed": (i32, [vp, vp, i64, i64, vp, i64, vp]),
     "fdk_gemm_bf16": (i32, [vp, i64, vp, i64, vp, i64, i64, i64, i64, i32, vp]),
     "fdk_gemm_bf16_residual_add": (i32, [vp, i64, vp, i64, vp, i64, i64, i64, i64, i32, vp, vp]),
+    "fdk_gemm_bf16_partials": (i32, [vp, i64, vp, i64, vp, i64, i64, i64, i32, vp]),
+    "fdk_rmsnorm_add_partials": (i32, [vp, i32, vp, i64, vp, i32, vp, i64, i64, i64, f32, f32, vp]),
     "fdk_gemm_bf16_qk_norm_rope": (i32, [vp, i64, vp, i64, vp, i64, i64, i64, i64, i64, i64, i64, vp, vp, vp, vp, i64,
                                          i32, f32, vp, vp, vp]),
     "fdk_swiglu": (i32, [vp, i64, vp, i64, i64, vp]),

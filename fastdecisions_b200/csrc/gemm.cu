@@ -39,7 +39,7 @@ constexpr int THREADS = 192;
 constexpr uint32_t TM_COLS = 512;
 constexpr long long DRAIN_BUDGET = 2000000000LL;
 
-enum Epi { PLAIN = 0, SWIGLU = 1, QKNORM128 = 2, QKNORM256 = 3, RESADD = 4 };
+enum Epi { PLAIN = 0, SWIGLU = 1, QKNORM128 = 2, QKNORM256 = 3, RESADD = 4, PARTIAL = 5 };
 
 __device__ int g_gemm_error = 0;
 
@@ -318,6 +318,34 @@ gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUte
           asm volatile("st.release.gpu.global.b32 [%0], %1;\n" ::"l"(ticket), "r"(next) : "memory");
         }
         __syncwarp();
+      } else if constexpr (EPI == PARTIAL) {
+        // k-slice `slice` of the tile -> plane `slice` of C ([k_split][m][n] float32, a 3-D map with
+        // [32 rows][32 fp32] boxes, 128-byte swizzle): plain TMA stores, no ordering between slices
+        const int slice = u - t * p.k_split;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tacc + c * 32, v);
+          tmem_ld_wait();
+          if (c == BN / 32 - 1) {
+            tc_fence_before();
+            mbar_arrive(bar(B_TEMPTY + acc));
+          }
+          const int b = pieces & 1;
+          if (lane == 0 && pieces >= 2) bulk_wait_read<1>();
+          __syncwarp();
+          uint8_t* dst = obuf_g + b * OUT_BOX + lane * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<uint4*>(dst + ((j ^ (lane & 7)) << 4)) = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&tc, obuf + b * OUT_BOX, nb * BN + c * 32, y, slice);
+            bulk_commit();
+          }
+          ++pieces;
+        }
       } else if constexpr (EPI == SWIGLU) {
 #pragma unroll 1
         for (int c = 0; c < BN / 128; ++c) {
@@ -658,4 +686,54 @@ extern "C" int fdk_gemm_bf16_residual_add(const void* a, int64_t lda, const void
   if (int st = ensure_smem_attr((const void*)gemm_kernel<RESADD>, (int)SMEM_BYTES, "gemm_residual_add")) return st;
   gemm_kernel<RESADD><<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ma, mb, mh, mh, mh, p);
   return check_launch("gemm_residual_add");
+}
+
+extern "C" int fdk_gemm_bf16_partials(const void* a, int64_t lda, const void* b, int64_t ldb, float* partials,
+                                      int64_t m, int64_t n, int64_t k, int slices, void* stream) {
+  using namespace fdk::gemm;
+  if (int st = check_device()) return st;
+  if (!a || !b || !partials) return set_error(FDK_ERR_INVALID_ARGUMENT, "gemm_partials: null pointer");
+  if (m < 0 || n <= 0 || k <= 0 || m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff)
+    return set_error(FDK_ERR_INVALID_ARGUMENT, "gemm_partials: bad sizes");
+  if (slices < 1 || slices > 16) return set_error(FDK_ERR_INVALID_ARGUMENT, "gemm_partials: slices in [1, 16]");
+  if (n % 8 || k % 8) return set_error(FDK_ERR_ALIGNMENT, "gemm_partials: n and k must be multiples of 8");
+  if (lda < k || ldb < k) return set_error(FDK_ERR_INVALID_ARGUMENT, "gemm_partials: row stride too small");
+  if (!aligned16(a) || !aligned16(b) || !aligned16(partials) || lda % 8 || ldb % 8)
+    return set_error(FDK_ERR_ALIGNMENT, "gemm_partials: pointers and row strides must be 16-byte aligned");
+  if (m == 0) return FDK_OK;
+  Params p{};
+  p.m = (int)m;
+  p.n = (int)n;
+  p.k = (int)k;
+  p.m_tiles = (int)((m + BM - 1) / BM);
+  p.n_tiles = (int)((n + BN - 1) / BN);
+  p.k_steps = (int)((k + BK - 1) / BK);
+  p.band = 8;
+  int s = slices > p.k_steps ? p.k_steps : slices;
+  p.kps = (p.k_steps + s - 1) / s;
+  p.k_split = (p.k_steps + p.kps - 1) / p.kps;  // every slice non-empty
+  if (p.k_split != slices)
+    return set_error(FDK_ERR_UNSUPPORTED, "gemm_partials: %d slices of %d k-steps leave one empty; use %d", slices,
+                     p.k_steps, p.k_split);
+  CUtensorMap ma, mb, mp;
+  if (int st = kmajor_map(&ma, a, m, k, lda, BM)) return st;
+  if (int st = kmajor_map(&mb, b, n, k, ldb, BN)) return st;
+  {  // [slices][m][n] float32, box 32 x 32 x 1, 128-byte swizzle
+    EncodeFn enc = encode_fn();
+    if (!enc) return set_error(FDK_ERR_DEVICE, "gemm_partials: cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[3] = {(cuuint64_t)n, (cuuint64_t)m, (cuuint64_t)slices};
+    cuuint64_t strides[2] = {(cuuint64_t)n * 4, (cuuint64_t)m * n * 4};
+    cuuint32_t box[3] = {32, 32, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(&mp, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, partials, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(FDK_ERR_INVALID_ARGUMENT, "gemm_partials: tensor map encode failed (%d)", (int)r);
+  }
+  const int64_t units = (int64_t)p.m_tiles * p.n_tiles * p.k_split;
+  if (units > 0x7fffffff) return set_error(FDK_ERR_UNSUPPORTED, "gemm_partials: too many tiles");
+  const int grid = (int)(units < sm_count() ? units : sm_count());
+  if (int st = ensure_smem_attr((const void*)gemm_kernel<PARTIAL>, (int)SMEM_BYTES, "gemm_partials")) return st;
+  gemm_kernel<PARTIAL><<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ma, mb, mp, mp, mp, p);
+  return check_launch("gemm_partials");
 }

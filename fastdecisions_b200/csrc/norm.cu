@@ -119,6 +119,67 @@ static void launch_rms_any(bool res32, bool has_res, bool w32, dim3 grid, cudaSt
 }
 
 // ---------------------------------------------------------------------------------------------
+// The residual add of k-split GEMM partials, then RMSNorm: one row per 128-thread warp group,
+// s = h + p_0 + ... + p_{nparts-1} in that order (float32), written back to h, and
+// out = bf16(s * rsqrt(mean(s^2) + eps) * (woff + w)) unless out is null.
+// ---------------------------------------------------------------------------------------------
+template <int NC, bool W_FP32>
+__global__ void __launch_bounds__(128) rmsnorm_add_partials_kernel(
+    const float* __restrict__ parts, int nparts, int64_t plane, float* __restrict__ h, int64_t ldh,
+    const void* __restrict__ w, bf16* __restrict__ out, int64_t ldo, int hidden, float eps, float woff) {
+  const int64_t row = blockIdx.x;
+  const int nvec = hidden >> 3;
+  float v[NC][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int i = threadIdx.x + c * 128;
+    if (i < nvec) {
+      float* hp = h + row * ldh + i * 8;
+      float4 a = *reinterpret_cast<const float4*>(hp), b = *reinterpret_cast<const float4*>(hp + 4);
+      v[c][0] = a.x; v[c][1] = a.y; v[c][2] = a.z; v[c][3] = a.w;
+      v[c][4] = b.x; v[c][5] = b.y; v[c][6] = b.z; v[c][7] = b.w;
+      for (int sidx = 0; sidx < nparts; ++sidx) {
+        const float* pp = parts + sidx * plane + row * (int64_t)hidden + i * 8;
+        const float4 pa = __ldcs(reinterpret_cast<const float4*>(pp)), pb = __ldcs(reinterpret_cast<const float4*>(pp + 4));
+        v[c][0] += pa.x; v[c][1] += pa.y; v[c][2] += pa.z; v[c][3] += pa.w;
+        v[c][4] += pb.x; v[c][5] += pb.y; v[c][6] += pb.z; v[c][7] += pb.w;
+      }
+      *reinterpret_cast<float4*>(hp) = make_float4(v[c][0], v[c][1], v[c][2], v[c][3]);
+      *reinterpret_cast<float4*>(hp + 4) = make_float4(v[c][4], v[c][5], v[c][6], v[c][7]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(v[c][j], v[c][j], ss);
+    }
+  }
+  if (out == nullptr) return;  // uniform: the add only
+  __shared__ float red[4];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  ss = (red[0] + red[1]) + (red[2] + red[3]);
+  const float inv = rsqrtf(ss / (float)hidden + eps);
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int i = threadIdx.x + c * 128;
+    if (i < nvec) {
+      float wv[8];
+      if (W_FP32) {
+        const float4* wp = reinterpret_cast<const float4*>(static_cast<const float*>(w) + i * 8);
+        float4 a = __ldg(wp), b = __ldg(wp + 1);
+        wv[0] = a.x; wv[1] = a.y; wv[2] = a.z; wv[3] = a.w;
+        wv[4] = b.x; wv[5] = b.y; wv[6] = b.z; wv[7] = b.w;
+      } else {
+        unpack8(__ldg(reinterpret_cast<const uint4*>(static_cast<const bf16*>(w) + i * 8)), wv);
+      }
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = v[c][j] * inv * (woff + wv[j]);
+      *reinterpret_cast<uint4*>(out + row * ldo + i * 8) = pack8(o);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
 // Gated RMSNorm per head row (dv = 128): 16 lanes per row, one 16-byte chunk of o and z each.
 // ---------------------------------------------------------------------------------------------
 template <bool W_FP32>
@@ -339,4 +400,32 @@ extern "C" int fdk_attn_qk_norm_rope(const void* qkv, int64_t ld_qkv, const void
     else qk_norm_rope_kernel<8, false><<<grid, 256, 0, s>>>(in, ld_qkv, q_norm_w, k_norm_w, positions, rope_table, (int)max_pos, rot_dim, qo, ko, tokens, (int)hq, (int)hkv, eps);
   }
   return check_launch("attn_qk_norm_rope");
+}
+
+extern "C" int fdk_rmsnorm_add_partials(const float* partials, int nparts, float* h, int64_t ldh, const void* weight,
+                                        int weight_is_fp32, void* out, int64_t ld_out, int64_t rows, int64_t hidden,
+                                        float eps, float weight_offset, void* stream) {
+  if (int st = check_device()) return st;
+  if (!partials || !h || (out && !weight)) return set_error(FDK_ERR_INVALID_ARGUMENT, "rmsnorm_add_partials: null pointer");
+  if (nparts < 1 || nparts > 16) return set_error(FDK_ERR_INVALID_ARGUMENT, "rmsnorm_add_partials: nparts in [1, 16]");
+  if (rows < 0 || hidden <= 0 || hidden % 8 != 0 || hidden > 4096)
+    return set_error(FDK_ERR_UNSUPPORTED, "rmsnorm_add_partials: hidden must be a positive multiple of 8 <= 4096");
+  if (ldh < hidden || (out && ld_out < hidden)) return set_error(FDK_ERR_INVALID_ARGUMENT, "rmsnorm_add_partials: row stride too small");
+  if (!aligned16(partials) || !aligned16(h) || ldh % 4 || (out && (!aligned16(out) || ld_out % 8 || !aligned16(weight))))
+    return set_error(FDK_ERR_ALIGNMENT, "rmsnorm_add_partials: pointers and row strides must be 16-byte aligned");
+  if (rows == 0) return FDK_OK;
+  if (rows > 0x7fffffff) return set_error(FDK_ERR_UNSUPPORTED, "rmsnorm_add_partials: too many rows");
+  const dim3 grid((unsigned)rows);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t plane = rows * hidden;
+  auto ob = static_cast<bf16*>(out);
+  const int nc = (int)((hidden / 8 + 127) / 128);
+  if (nc <= 2) {
+    if (weight_is_fp32) rmsnorm_add_partials_kernel<2, true><<<grid, 128, 0, s>>>(partials, nparts, plane, h, ldh, weight, ob, ld_out, (int)hidden, eps, weight_offset);
+    else rmsnorm_add_partials_kernel<2, false><<<grid, 128, 0, s>>>(partials, nparts, plane, h, ldh, weight, ob, ld_out, (int)hidden, eps, weight_offset);
+  } else {
+    if (weight_is_fp32) rmsnorm_add_partials_kernel<4, true><<<grid, 128, 0, s>>>(partials, nparts, plane, h, ldh, weight, ob, ld_out, (int)hidden, eps, weight_offset);
+    else rmsnorm_add_partials_kernel<4, false><<<grid, 128, 0, s>>>(partials, nparts, plane, h, ldh, weight, ob, ld_out, (int)hidden, eps, weight_offset);
+  }
+  return check_launch("rmsnorm_add_partials");
 }

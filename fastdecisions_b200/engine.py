@@ -107,7 +107,8 @@ def plan_batches(lengths: Sequence[int], max_tokens: int) -> list:
 class DecisionEngine:
     def __init__(self, cfg: ModelConfig, weights: dict, device="cuda", letter_ids=LETTER_IDS,
                  temperature: float = 1.0, residual_fp32: bool = True, fuse_gdn_prologue: bool = True,
-                 fused_swiglu_gemm: bool = True, fused_qkv_gemm: bool = False, fused_residual_gemm: bool = True):
+                 fused_swiglu_gemm: bool = True, fused_qkv_gemm: bool = False, fused_residual_gemm: bool = True,
+                 split_residual_gemm: bool = False):
         """``residual_fp32`` keeps the residual stream in float32 (the sum of the layer outputs is
         never rounded); with False it is stored in bf16 like the eager bf16 model.
         ``fuse_gdn_prologue`` runs the Gated-DeltaNet conv, gates and delta rule as one call on the
@@ -129,7 +130,12 @@ class DecisionEngine:
         outputs are never rounded to bf16 and the norm moves 6 bytes an element instead of 12.
         Measured at 32k tokens: out-projection + norm 423 -> 294 us, down-projection + norm
         741 -> 633 us, +1.1% requests/s on config 5; at batch 1 (1536 tokens) cuBLAS and the
-        fused residual-add RMSNorm stay faster (5.21 vs 5.46 ms)."""
+        fused residual-add RMSNorm stay faster (5.21 vs 5.46 ms).
+        ``split_residual_gemm`` (float32 stream) runs those projections of smaller batches, where
+        the output tiles leave SMs idle, as K-split GEMMs writing fp32 partial planes that the next
+        RMSNorm adds into the stream in a fixed order (reproducible; no bf16 rounding of the layer
+        output).  Off by default: measured slower than cuBLAS + the residual-add RMSNorm in the
+        config-4 graph (5.77 vs 5.30 ms)."""
         self.cfg = cfg
         self.fuse_gdn_prologue = bool(fuse_gdn_prologue)
         self.fused_swiglu_gemm = bool(fused_swiglu_gemm)
@@ -137,6 +143,7 @@ class DecisionEngine:
         self.residual_fp32 = bool(residual_fp32)
         self.fused_residual_gemm = bool(fused_residual_gemm) and self.residual_fp32
         self.residual_split_k = 0  # k-slices of the residual-add GEMMs (0: the library's choice)
+        self.split_residual_gemm = bool(split_residual_gemm) and self.residual_fp32
         self.dev = torch.device(device)
         self.temperature = float(temperature)
         dev = self.dev
@@ -182,6 +189,7 @@ class DecisionEngine:
             self.layers.append(L)
         self._ws: dict = {}
         self._tk: dict = {}
+        self._parts: dict = {}
         self._graphs = {}
         self._graph_pool = None
         self._sealed = False
@@ -211,6 +219,16 @@ class DecisionEngine:
             tk = torch.zeros(need, device=self.dev, dtype=torch.int32)
             self._tk[key] = tk
         return tk
+
+    def _partials(self, tokens: int, slices: int) -> torch.Tensor:
+        """float32 k-slice planes of the split projection GEMMs of the current stream."""
+        need = slices * tokens * self.cfg.hidden_size
+        key = torch.cuda.current_stream(self.dev).cuda_stream
+        buf = self._parts.get(key)
+        if buf is None or buf.numel() < need:
+            buf = torch.empty(max(need, 4 * tokens * self.cfg.hidden_size), device=self.dev, dtype=torch.float32)
+            self._parts[key] = buf
+        return buf
 
     def reserve(self, tokens: int, segments: int):
         """Pre-size the delta-rule scratch and the GEMM tickets (call before graph capture)."""
@@ -274,7 +292,15 @@ class DecisionEngine:
                 o = ops.gqa_attention_varlen_(q, k, v, cu, max_seqlen, gate=proj[:, D:], gate_interleaved=True)
             mix_in, w_mix = o.view(T, hq * D), L.w_o
         fused_res = self.fused_residual_gemm and T >= FUSED_RESIDUAL_MIN_TOKENS
-        if fused_res:  # out-projection adds into the fp32 stream; then its norm alone
+        H = c.hidden_size
+        split_mix = 0 if fused_res or not self.split_residual_gemm else ops.split_slices(T, H, mix_in.shape[1])
+        split_down = 0 if fused_res or not self.split_residual_gemm else ops.split_slices(T, H, c.intermediate_size)
+        if split_mix > 1:  # k-split partial planes, added into the stream in order by the norm
+            with tm("gemm_partials"):
+                parts = ops.gemm_partials(mix_in, w_mix, self._partials(T, split_mix), split_mix)
+            with tm("residual_rmsnorm"):
+                x2 = ops.rmsnorm_add_partials(parts, split_mix, h, L.post_norm, c.rms_norm_eps)
+        elif fused_res:  # out-projection adds into the fp32 stream; then its norm alone
             with tm("gemm_residual_add"):
                 ops.gemm_residual_add(mix_in, w_mix, h, split_k=self.residual_split_k, tickets=self._tickets(T))
             with tm("residual_rmsnorm"):
@@ -292,6 +318,10 @@ class DecisionEngine:
                 gu = torch.matmul(x2, L.w_gu.t())
             with tm("swiglu"):
                 act = ops.swiglu(gu, c.intermediate_size)
+        if split_down > 1:  # partial planes; the caller's norm (or the readout's add) sums them in
+            with tm("gemm_partials"):
+                ops.gemm_partials(act, L.w_down, self._partials(T, split_down), split_down)
+            return ("partials", split_down)
         if fused_res:  # the MLP output goes straight into the stream: nothing returned
             with tm("gemm_residual_add"):
                 ops.gemm_residual_add(act, L.w_down, h, split_k=self.residual_split_k, tickets=self._tickets(T))
@@ -317,6 +347,16 @@ class DecisionEngine:
         down = None
         for i in range(len(self.layers)):
             down = self._mixer_mlp(i, x, h, cu, pos, max_seqlen, ws)
+            if isinstance(down, tuple):  # k-split partial planes of the down-projection
+                parts = self._partials(h.shape[0], down[1])
+                with tm("residual_rmsnorm"):
+                    x = ops.rmsnorm_add_partials(parts, down[1], h, self.layers[i + 1].in_norm if i + 1 < len(
+                        self.layers) else None, c.rms_norm_eps)
+                down = None
+                if i + 1 < len(self.layers):
+                    if trace is not None:
+                        trace.append(h.clone())
+                    continue
             if i + 1 < len(self.layers):
                 with tm("residual_rmsnorm"):
                     if down is None:  # already added into h by the down-projection
@@ -342,6 +382,9 @@ class DecisionEngine:
         zero = torch.zeros(h.shape, device=self.dev, dtype=torch.bfloat16)
         x, _ = ops.residual_rmsnorm(zero, h, self.layers[i].in_norm, c.rms_norm_eps, residual_out=h)
         down = self._mixer_mlp(i, x, h, cu, pos, max_seqlen, self._workspace(h.shape[0], cu.numel() - 1))
+        if isinstance(down, tuple):
+            ops.rmsnorm_add_partials(self._partials(h.shape[0], down[1]), down[1], h, None)
+            down = None
         return h.float() + (0.0 if down is None else down.float())
 
     # ------------------------------------------------------------------ host API

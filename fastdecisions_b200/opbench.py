@@ -242,10 +242,11 @@ def main(argv=None):
                     help="attention geometry hq,hkv,head_dim (e.g. 8,2,256: the reference kernel's own shape)")
     ap.add_argument("--cublas", action="store_true", help="gemm_* ops: time torch.matmul (cuBLAS) instead")
     ap.add_argument("--replays", type=int, default=30, help="--op forward_cfg4: graph replays")
-    ap.add_argument("--split-k", type=int, default=0, help="--op forward_cfg4: k-slices of the residual-add GEMMs")
+    ap.add_argument("--split-k", type=int, default=0,
+                    help="--op forward_cfg4: 1 = out / down projections as k-split partial GEMMs (default: cuBLAS)")
     args = ap.parse_args(argv)
     if args.op == "forward_cfg4":
-        forward_cfg4(args.replays, fused_residual_gemm=not args.cublas, residual_split_k=args.split_k)
+        forward_cfg4(args.replays, split_residual_gemm=args.split_k != 0, residual_split_k=0)
         return
     global CUBLAS
     CUBLAS = args.cublas

@@ -637,3 +637,52 @@ def gemm_residual_add(a: torch.Tensor, w: torch.Tensor, h: torch.Tensor, split_k
                   w.stride(0) if n > 1 else k, h.data_ptr(), h.stride(0) if m > 1 else n, m, n, k, int(split_k),
                   tickets.data_ptr(), _stream(a))
     return h
+
+
+def split_slices(m: int, n: int, k: int, sms: int = 148, max_slices: int = 4) -> int:
+    """K-slices for ``gemm_partials``: the count (every slice non-empty) minimising waves of
+    (tile, slice) units over the SMs x (k-steps a unit + 2 for its epilogue); 1 when the
+    128 x 256 output tiles alone fill the SMs."""
+    tiles = ((m + 127) // 128) * ((n + 255) // 256)
+    steps = (k + 63) // 64
+    best, best_cost = 1, None
+    for s in range(1, min(max_slices, steps) + 1):
+        kps = -(-steps // s)
+        if -(-steps // kps) != s:
+            continue
+        cost = -(-tiles * s // sms) * (kps + 2)
+        if best_cost is None or cost < best_cost:
+            best, best_cost = s, cost
+    return best
+
+
+def gemm_partials(a: torch.Tensor, w: torch.Tensor, partials: torch.Tensor, slices: int) -> torch.Tensor:
+    """``partials[s] = a[:, K_s] @ w[:, K_s]^T`` (float32 planes ``[slices, m, n]``) for the ``slices``
+    parts of K; ``rmsnorm_add_partials`` adds them into the residual stream in order."""
+    _need_cuda(a, w, partials)
+    m, k = a.shape
+    n = w.shape[0]
+    if a.dtype != BF16 or w.dtype != BF16 or w.shape[1] != k or a.stride(1) != 1 or w.stride(1) != 1:
+        raise ValueError("gemm_partials: a [m, k] and w [n, k] must be bf16 with unit column stride")
+    if partials.dtype != torch.float32 or not partials.is_contiguous() or partials.numel() < slices * m * n:
+        raise ValueError("gemm_partials: partials must be contiguous float32 with room for [slices, m, n]")
+    with torch.cuda.device(a.device):
+        _lib.call("fdk_gemm_bf16_partials", a.data_ptr(), a.stride(0) if m > 1 else k, w.data_ptr(),
+                  w.stride(0) if n > 1 else k, partials.data_ptr(), m, n, k, int(slices), _stream(a))
+    return partials
+
+
+def rmsnorm_add_partials(partials: torch.Tensor, slices: int, h: torch.Tensor, weight: Optional[torch.Tensor],
+                         eps: float = 1e-6, weight_offset: float = 1.0) -> Optional[torch.Tensor]:
+    """``h += partials[0] + ... + partials[slices - 1]`` (in that order), then the RMSNorm of ``h``
+    (bf16, returned) -- or only the add when ``weight`` is None."""
+    _need_cuda(partials, h, weight)
+    rows, H = h.shape
+    if h.dtype != torch.float32 or h.stride(1) != 1 or partials.dtype != torch.float32:
+        raise ValueError("rmsnorm_add_partials: float32 h and partials expected")
+    out = None if weight is None else torch.empty((rows, H), device=h.device, dtype=BF16)
+    with torch.cuda.device(h.device):
+        _lib.call("fdk_rmsnorm_add_partials", partials.data_ptr(), int(slices), h.data_ptr(),
+                  h.stride(0) if rows > 1 else H, _ptr(weight), int(weight is not None and weight.dtype == torch.float32),
+                  _ptr(out), H, rows, H, float(eps), float(weight_offset), _stream(h))
+    return out

@@ -293,6 +293,30 @@ int fdk_gemm_bf16_residual_add(const void* a, int64_t lda, const void* b, int64_
                                int64_t ldh, int64_t m, int64_t n, int64_t k, int split_k,
                                int32_t* tickets, void* stream);
 
+/*
+ * Projection GEMM split along K into `slices` parts whose fp32 products land in separate planes:
+ * partials [slices][m][n] (contiguous float32), plane s = A[:, K_s] B[:, K_s]^T over the s-th
+ * slice of K.  For the out / down projections at batch-1 sizes, where the output tiles alone leave
+ * SMs idle (m = 1536, n = 2048: 96 tiles for 148 SMs); fdk_rmsnorm_add_partials then adds the
+ * planes into the residual stream in a fixed order ([tf]:775, 781), so results are reproducible and
+ * the layer output is never rounded to bf16 (measured: in the config-4 forward this pair is
+ * slower than a cuBLAS GEMM + fdk_residual_rmsnorm, 5.77 vs 5.30 ms).  Every slice must be non-empty
+ * (slices <= ceil(k / 64), and no slice left empty by rounding); n and k multiples of 8.
+ */
+int fdk_gemm_bf16_partials(const void* a, int64_t lda, const void* b, int64_t ldb, float* partials,
+                           int64_t m, int64_t n, int64_t k, int slices, void* stream);
+
+/*
+ * h [rows, hidden] (float32) += partials[0] + ... + partials[nparts - 1] (planes of
+ * [rows][hidden] float32, added in that order), then out = bf16(h * rsqrt(mean(h^2) + eps) *
+ * (weight_offset + w)) when out is non-NULL ([tf]:711-728 after the residual add of [tf]:775 /
+ * 781).  hidden a multiple of 8, at most 4096.
+ */
+int fdk_rmsnorm_add_partials(const float* partials, int nparts, float* h, int64_t ldh,
+                             const void* weight, int weight_is_fp32, void* out, int64_t ld_out,
+                             int64_t rows, int64_t hidden, float eps, float weight_offset,
+                             void* stream);
+
 /* Token embedding gather: out[t, :] = table[ids[t], :] ([tf]:1243).  ids int32. */
 int fdk_embed(const int32_t* ids, const void* table, int64_t vocab, int64_t hidden, void* out,
               int64_t tokens, void* stream);

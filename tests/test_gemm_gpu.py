@@ -132,3 +132,38 @@ def test_gemm_residual_add_is_reproducible_with_split_k():
     assert _lib.poll_device_error() == 0
     assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
     assert int(tk.abs().sum()) == 0
+
+
+@pytest.mark.parametrize("m,n,k", [(1536, 2048, 2048), (1536, 2048, 6144), (300, 264, 136), (5, 2048, 6144)])
+def test_gemm_partials_and_ordered_add(m, n, k):
+    """k-split planes from the GEMM, added into the float32 stream in a fixed order by the norm
+    kernel: h + a w^T against the float32 product, the norm against the oracle, and repeat calls
+    bit-identical."""
+    a, w = inputs(m, n, k, 5 * m + n + k)
+    s = ops.split_slices(m, n, k)
+    if n == 264:
+        s = 2
+    h0 = torch.randn(m, n, generator=torch.Generator().manual_seed(k))
+    nw = (0.02 * torch.randn(n, generator=torch.Generator().manual_seed(n))).bfloat16()
+    parts = torch.empty(s * m * n, device="cuda", dtype=torch.float32)
+    outs = []
+    for _ in range(2):
+        h = h0.cuda()
+        ops.gemm_partials(a.cuda(), w.cuda(), parts, s)
+        x = ops.rmsnorm_add_partials(parts, s, h, nw.cuda())
+        outs.append((h.clone(), x))
+    torch.cuda.synchronize()
+    assert _lib.poll_device_error() == 0
+    ref = h0 + a.float() @ w.float().t()
+    err = (outs[0][0].cpu() - ref).abs().max().item()
+    assert err <= 1e-4 * max(1.0, ref.abs().max().item()), err
+    torch.testing.assert_close(outs[0][1].cpu().float(), O.rmsnorm_offset(ref, nw), rtol=0.008, atol=0.002)
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+    h = h0.cuda()
+    assert ops.rmsnorm_add_partials(parts, s, h, None) is None  # the add alone (last layer)
+    assert torch.equal(h, outs[0][0])
+
+
+def test_split_slices_choice():
+    assert ops.split_slices(1536, 2048, 2048) == 3 and ops.split_slices(1536, 2048, 6144) == 3
+    assert ops.split_slices(32768, 2048, 2048) == 1
