@@ -239,3 +239,15 @@ def test_bucketed_graphs_match_eager(cfg, weights):
     captures = eng.stats["graph_captures"]
     assert np.abs(eng.score(big, graphs=True) - eng.score(big)).max() == 0
     assert eng.stats["graph_captures"] == captures
+
+
+def test_bf16_residual_stream_engine(cfg, weights):
+    """residual_fp32=False: the residual stream stored in bf16 with the eager model's roundings
+    (cuBLAS projections and the residual-add RMSNorm for every batch size), against the oracle,
+    including a packed batch above the fused-GEMM size threshold."""
+    eng = DecisionEngine(cfg, weights, "cuda", residual_fp32=False)
+    assert not eng.fused_residual_gemm and not eng.split_residual_gemm
+    small = requests(cfg, ((70, 2), (150, 8), (33, 4), (1, 3)), seed=31)
+    check_decisions(eng.score(small), oracle_probs(cfg, weights, small), bound=0.05)
+    big = requests(cfg, ((2100, 4), (1900, 5), (300, 8)), seed=32)  # one packed batch of 4300 tokens
+    check_decisions(eng.score(big), oracle_probs(cfg, weights, big), bound=0.05)
